@@ -1,0 +1,355 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark: Qwen3-4B-shaped paged decode, batch 128, 36 layers.
+
+One step = one decode step of the model's attention: for each of 36 layers
+(each with its own paged KV cache, so no layer is served from L2) the
+split-KV paged decode over B=128 sequences with Hq=32, Hk=8, D=128, bf16,
+page size 16 and context lengths prompt U[128,1024] + generated U[1,256].
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``value`` is the whole-job KV HBM throughput
+(algorithmic K+V bytes of all ranks / max-over-ranks device time, GB/s) with
+inputs resident; ``e2e`` is the same metric through the public
+``flash_attn_with_kvcache`` with q copied from pinned host memory and every
+layer's output read back inside the timed region.  Multi-GPU runs are weak
+scaling: every rank decodes its own batch of 128 sequences, no collective on
+the data path.  ``--impl reference`` times the CPU oracle port (the
+reference's PyTorch-CPU algorithm restated in numpy) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+HQ, HKV, D, PS, BATCH, LAYERS = 32, 8, 128, 16, 128, 36
+METRIC = "decode-attn KV HBM GB/s & tok/s (Qwen3-4B shape, b128) at 1/2/4/8 B200"
+WORKLOAD = "qwen3-4b paged decode attention, b128, 36 layers (config 2)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- reference
+
+def cpu_oracle_sample(lengths, seed, n_seqs, dtype="bf16"):
+    """Host inputs for a bounded CPU sample: n_seqs sequences of one layer."""
+    import numpy as np
+
+    from mxflashattn_b200 import synthetic as syn
+
+    sel = [int(x) for x in lengths[:n_seqs]]
+    case = syn.paged_case(seed, batch=len(sel), q_heads=HQ, kv_heads=HKV, head_dim=D, dtype=dtype, page_size=PS,
+                          lengths=sel)
+    return case, syn.kv_bytes(sel, HKV, D)
+
+
+def time_cpu_oracle(case, reps: int):
+    import oracle
+
+    times = []
+    for _ in range(reps):
+        kc, vc, sl = case.k_cache, case.v_cache, case.cache_seqlens.copy()
+        t0 = time.perf_counter()
+        oracle.attention_kvcache(case.q, kc, vc, cache_seqlens=sl, block_table=case.block_table,
+                                 softmax_scale=case.softmax_scale)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm (oracle port) on this host's cores."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from mxflashattn_b200 import synthetic as syn
+
+    lengths = syn.qwen3_4b_lengths(args.seed, args.batch)
+    n_seqs = 16
+    case, nbytes = cpu_oracle_sample(lengths, args.seed, n_seqs)
+    time_cpu_oracle(case, max(1, min(args.warmup, 3)))
+    times = time_cpu_oracle(case, args.steps)
+    sec = sum(times) / len(times)
+    gbs = nbytes / sec / 1e9
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
+                   "head_dim": D, "page_size": PS,
+                   "sample": f"{n_seqs} of {args.batch} sequences of one layer per step"},
+        "tok_per_s": n_seqs / sec / args.layers,
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_seqs} sequences x 1 layer per step, numpy fp32 on {cpu_model()}"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- ours
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_env()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+
+    from mxflashattn_b200 import backend, flash_attn_with_kvcache, synthetic as syn
+
+    lengths = syn.qwen3_4b_lengths(args.seed + rank, args.batch)
+    layers = []
+    for layer in range(args.layers):
+        layers.append(syn.device_paged_decode(seed=1000 * (rank + 1) + layer, lengths=lengths, q_heads=HQ,
+                                              kv_heads=HKV, head_dim=D, dtype="bf16", page_size=PS,
+                                              device=device))
+    torch.cuda.synchronize(device)
+    bytes_layer = syn.kv_bytes(lengths, HKV, D)
+    bytes_step = bytes_layer * args.layers
+    max_len = layers[0]["block_table"].shape[1] * PS
+    num_splits, chunk_len = backend.kvcache_plan(args.batch, 1, HQ, HKV, D, max_len)
+    launches_per_layer = 2 if num_splits > 1 else 1
+    scale = D ** -0.5
+    outs = [torch.empty_like(t["q"]) for t in layers]
+    stream = torch.cuda.current_stream(device)
+
+    def step(ev=None):
+        for i, t in enumerate(layers):
+            if ev is not None:
+                ev[2 * i].record(stream)
+            backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                      scale, False, num_splits=num_splits, chunk_len=chunk_len, out=outs[i])
+            if ev is not None:
+                ev[2 * i + 1].record(stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+
+    layer_events = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * args.layers)]
+                    for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        t_start.record(stream)
+        for s in range(args.steps):
+            step(layer_events[s])
+        t_end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    launch_ms = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for evs in layer_events for i in range(args.layers)]
+    per_launch_ms = sum(launch_ms) / len(launch_ms)
+    if dist is not None:
+        tt = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    ms_step = elapsed_ms / args.steps
+    value = world * bytes_step / (ms_step * 1e-3) / 1e9
+    tok_s = world * args.batch / (ms_step * 1e-3)
+
+    # --------------------------------------------------------------- e2e
+    e2e = None
+    if not args.no_e2e:
+        q_host = [t["q"].cpu().pin_memory() for t in layers]
+        out_host = [torch.empty_like(q, pin_memory=True) for q in q_host]
+        sl_host = layers[0]["cache_seqlens"].cpu().pin_memory()
+        q_dev = [torch.empty_like(t["q"]) for t in layers]
+        sl_dev = torch.empty_like(layers[0]["cache_seqlens"])
+
+        def e2e_step_tables():
+            # per step: upload the lengths once and each layer's q, read each layer's output back
+            sl_dev.copy_(sl_host, non_blocking=True)
+            for i, t in enumerate(layers):
+                q_dev[i].copy_(q_host[i], non_blocking=True)
+                o = flash_attn_with_kvcache(q_dev[i], t["k_cache"], t["v_cache"], cache_seqlens=sl_dev,
+                                            block_table=t["block_table"], softmax_scale=scale)
+                out_host[i].copy_(o, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step_tables()
+        torch.cuda.synchronize(device)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step_tables()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        e_ms = e0.elapsed_time(e1)
+        if dist is not None:
+            tt = torch.tensor([e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e_ms = float(tt.item())
+        e_step = e_ms / args.steps
+        q_bytes = sum(q.numel() * q.element_size() for q in q_host)
+        e2e = {"value": world * bytes_step / (e_step * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": q_bytes + sl_host.numel() * 4,
+               "d2h_bytes_per_step": sum(o.numel() * o.element_size() for o in out_host),
+               "ms_per_step": e_step, "tok_per_s": world * args.batch / (e_step * 1e-3)}
+
+    # ------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        case, nbytes = cpu_oracle_sample(lengths, args.seed, 16)
+        time_cpu_oracle(case, 1)
+        times = time_cpu_oracle(case, 3)
+        sec = sum(times) / len(times)
+        cpu = {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"16 of {args.batch} sequences x 1 layer, numpy fp32 oracle, 3 reps on {cpu_model()}"}
+
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_layer / (per_launch_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
+                   "head_dim": D, "page_size": PS, "mean_ctx": float(sum(lengths)) / len(lengths),
+                   "num_splits": num_splits, "chunk_len": chunk_len,
+                   "l2": f"inputs larger than L2: {args.layers} distinct layer caches, "
+                         f"{bytes_step / 1e9:.1f} GB read per step",
+                   "parallelism": f"dp{world} (independent batches, no collective)"},
+        "tok_per_s": tok_s,
+        "e2e": e2e,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "paged_decode_kernel" + (" + split_combine_kernel" if num_splits > 1 else ""),
+                     "bytes_per_launch": bytes_layer, "avg_launch_ms": per_launch_ms},
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps * args.layers * launches_per_layer,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/*
+ * mxfa_b200.h -- C ABI of libmxfa_b200.so, the sm_100a (B200) kernels behind
+ * MXFlashAttn's decode and prefill hot path.
+ *
+ * Conventions
+ *  - Every entry point is stream-ordered and asynchronous on `stream` (a
+ *    cudaStream_t passed as void*; NULL = legacy default stream).  None of
+ *    them synchronises the device or reads device memory on the host, so a
+ *    caller may record them inside a CUDA graph.
+ *  - The caller owns and allocates every buffer, including split workspaces
+ *    (sizes from the *_workspace_bytes helpers).  Pointers are raw device
+ *    pointers to contiguous row-major tensors.
+ *  - Return value: MXFA_OK (0) on success; MXFA_ERR_UNSUPPORTED (-1) for a
+ *    configuration the kernels do not cover (the same -1 the reference's
+ *    launchers return); MXFA_ERR_INVALID (-2) for a bad argument;
+ *    MXFA_ERR_CUDA (-3) when the launch itself failed.  mxfa_last_error()
+ *    returns a thread-local description of the last non-zero status.
+ *  - Element type: `bf16` = 1 for bfloat16, 0 for float16.  Arithmetic is
+ *    fp32 (softmax, accumulation); outputs are rounded to nearest-even.
+ *  - Stateless and re-entrant; the only module state is the device-side
+ *    error word read by mxfa_read_error_flags().
+ */
+#ifndef MXFA_B200_H_
+#define MXFA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MXFA_OK 0
+#define MXFA_ERR_UNSUPPORTED (-1)
+#define MXFA_ERR_INVALID (-2)
+#define MXFA_ERR_CUDA (-3)
+
+/* Device error flags (bitwise OR) raised by kernels instead of faulting. */
+#define MXFA_FLAG_PAGE_OUT_OF_RANGE 0x1u  /* block-table entry outside [0, num_pages) */
+#define MXFA_FLAG_TABLE_TOO_NARROW 0x2u   /* sequence longer than block_table width * page size */
+#define MXFA_FLAG_WAIT_TIMEOUT 0x4u       /* a bounded pipeline wait gave up */
+#define MXFA_FLAG_DENSE_OVERFLOW 0x8u     /* dense-cache append past the cache capacity */
+
+/* Library identity.  No reference counterpart (the reference's pybind
+ * modules expose no version); used by the ctypes loader. */
+int mxfa_abi_version(void);
+
+/* Thread-local text of the last failing call (empty string if none).
+ * Replaces the TORCH_CHECK messages of csrc_native/m1_binding.cpp:74,113. */
+const char* mxfa_last_error(void);
+
+/* 1 when the current CUDA device is sm_100 and the kernels can launch,
+ * else 0.  Replaces `is_available()` of the ATen extension
+ * (csrc/mxmac/attention_forward.cpp:98-100), which always returned true. */
+int mxfa_is_available(void);
+
+/* Read (and clear) the device error flags of the current device.
+ * Synchronises the device: diagnostics and tests only, never in a hot path. */
+int mxfa_read_error_flags(unsigned int* flags);
+
+/* ------------------------------------------------------------------ decode */
+
+/* Reference-compatible split-KV paged decode: same arguments, layouts and
+ * return codes as the MetaX launcher it replaces,
+ * mxfa_paged_decode_split_launch (csrc_native/m1_kernel.cpp:1206-1222).
+ *   q   [B, 1, HQ, D]          k, v  [P, PS, HKV, D]      (bf16 or fp16)
+ *   bt  int32 [B, BTW]         sl    int32 [B]
+ *   out [B, 1, HQ, D]          ows   f32 [B, HQ, NP, D]   mdws f32 [B, HQ, NP, 2]
+ * Chunk z covers positions [z*c_len, (z+1)*c_len) of each sequence; the
+ * partials hold the unnormalised sum of p*v, the log2-domain running max m
+ * and d = sum 2^(s - m), exactly the state the reference's split_combine
+ * (m1_kernel.cpp:862-888) merges, and this call runs that combine too.
+ * Guards as the reference: D in {64,128}, HQ % HKV == 0, GQ in {2,4,8},
+ * NP >= 1, else -1.  `um` (the reference's softmax-variant switch, 0/1/2)
+ * is accepted and validated; every variant is served by the same
+ * overflow-safe online softmax here. */
+int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt,
+                                   const void* sl, void* out, void* ows, void* mdws, float scale,
+                                   int B, int HQ, int HKV, int D, int PS, int BTW, int bf16, int NP,
+                                   int c_len, int um, void* stream);
+
+/* Bytes of split workspace (partials + (m,d) pairs) for `rows` query rows
+ * (rows = B * Sq * HQ) and NP splits.  No reference counterpart: the
+ * reference binding allocated these buffers itself (m1_binding.cpp:94-97). */
+size_t mxfa_split_workspace_bytes(int rows, int D, int NP);
+
+/* Split plan for flash_attn_with_kvcache on this GPU: number of splits and
+ * chunk length (positions) for sequences of at most `max_len` tokens, sized
+ * to the device's SM count.  Replaces the NP / c_len heuristic of the vLLM
+ * hook (integrations/vllm/vllm_plugin.py:271-276). */
+int mxfa_kvcache_plan(int B, int Sq, int HQ, int HKV, int D, int max_len, int* num_splits,
+                      int* chunk_len);
+
+/* KV-cache attention, the device path of flash_attn_with_kvcache
+ * (mxflashattn/api.py:151-286; reference semantics mxflashattn/reference.py:88-139
+ * with the append done separately by mxfa_kv_append_launch).
+ *   q        [B, Sq, HQ, D]
+ *   k_cache  paged [P, PS, HKV, D] (block_table != NULL) or dense [B, PS, HKV, D]
+ *   seqlens  int32 [B]: cached lengths BEFORE this call's append; the call
+ *            attends to seqlens[b] + append_len tokens
+ *   out      [B, Sq, HQ, D];  lse optional f32 [B, Sq, HQ] (natural log)
+ *   workspace f32, >= mxfa_split_workspace_bytes(B*Sq*HQ, D, num_splits)
+ *            bytes when num_splits > 1 (may be NULL when num_splits == 1)
+ * causal is bottom-right aligned (query i sees keys <= L - Sq + i).  Any
+ * GQ = HQ / HKV is accepted; D in {64, 128}. */
+int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* block_table, const int32_t* seqlens, void* out,
+                                  float* lse, void* workspace, size_t workspace_bytes, int B, int Sq,
+                                  int HQ, int HKV, int D, int PS, int BTW, int num_pages,
+                                  int append_len, int num_splits, int chunk_len, int causal,
+                                  int bf16, float scale, void* stream);
+
+/* LSE merge of split partials (the reference's split_combine,
+ * csrc_native/m1_kernel.cpp:862-888, generalised to strided partials).
+ * Partial p of row r lives at ows[r*NP*D + p*D] and mdws[(r*NP + p)*2].
+ * Writes out [rows, D] in bf16/fp16 when `out` != NULL, f32 [rows, D] when
+ * `out_f32` != NULL, and the natural-log LSE [rows] when `lse` != NULL. */
+int mxfa_split_combine_launch(const float* ows, const float* mdws, void* out, float* out_f32,
+                              float* lse, int rows, int D, int NP, int bf16, void* stream);
+
+/* Merge of per-rank (O, LSE) results for context-split decode across GPUs
+ * (no reference counterpart: the reference is single-device).  `packed` is
+ * f32 [N, rows, D + 1]: normalised O then the natural-log LSE of each row on
+ * each of N ranks (the buffer an all-gather produces).  Writes the merged
+ * out [rows, D] (bf16/fp16) and, if non-NULL, lse [rows]. */
+int mxfa_lse_merge_launch(const float* packed, void* out, float* lse, int N, int rows, int D,
+                          int bf16, void* stream);
+
+/* ------------------------------------------------------------------ append */
+
+/* Paged / dense KV append (reference.py:108-122): token i of sequence b
+ * goes to logical position seqlens[b] + i, i.e. page
+ * block_table[b, pos / PS], slot pos % PS (dense: row pos of cache b).
+ * Bit-exact copy.  Does not change seqlens (see mxfa_seqlens_add_launch).
+ *   k_new, v_new [B, Sk, HKV, D]; caches as in mxfa_kvcache_attention_launch.
+ * Out-of-range pages / capacity are skipped and flagged, never written. */
+int mxfa_kv_append_launch(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                          const int32_t* block_table, const int32_t* seqlens, int B, int Sk, int HKV,
+                          int D, int PS, int BTW, int num_pages, int elem_bytes, void* stream);
+
+/* seqlens[b] += delta on the device for int32 (is_int64 = 0) or int64
+ * lengths -- the in-place `cache_seqlens.add_(k.shape[1])` of
+ * reference.py:137-138 / dispatch.py:117-121, without a host sync. */
+int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void* stream);
+
+/* ----------------------------------------------------------------- prefill */
+
+/* Causal / non-causal attention forward over packed variable-length
+ * sequences: flash_attn_varlen_func (api.py:69-148, reference.py:60-85) and,
+ * with cu_q == cu_k == NULL, the dense flash_attn_func (api.py:34-66) with
+ * uniform lengths max_q / max_k per batch item.
+ *   q [Tq, HQ, D], k/v [Tk, HKV, D] (dense: [B, max_q|max_k, H, D])
+ *   cu_q, cu_k int32 [B + 1] device arrays (or NULL for dense)
+ *   out [Tq, HQ, D]; lse optional f32 [Tq, HQ]
+ * max_q must bound every q length (it sizes the grid). */
+int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q,
+                           const int32_t* cu_k, void* out, float* lse, int B, int max_q, int max_k,
+                           int HQ, int HKV, int D, int causal, int bf16, float scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXFA_B200_H_ */

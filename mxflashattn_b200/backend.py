@@ -1,0 +1,222 @@
+"""The single CUDA backend behind ``dispatch``: torch tensors -> libmxfa_b200.
+
+It exposes the extension contract the reference's dispatcher calls
+(``getattr(ext, operation)(*extension_args)`` guarded by ``is_available()``,
+mxflashattn/dispatch.py:131-137) with the positional argument lists the
+reference's public API builds (mxflashattn/api.py:53, :122-133, :251-262):
+
+* ``flash_attn_func(q, k, v, causal, scale)``
+* ``flash_attn_varlen_func(q, k, v, cu_q, cu_k, max_q, max_k, causal, scale)``
+* ``flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, scale, causal)``
+
+PyTorch is used for device buffers and the current stream only; all math
+runs in the sm_100a kernels.  Every call is asynchronous on the current
+stream and reads nothing back to the host.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
+
+
+def is_available() -> bool:
+    """True when a CUDA device of compute capability 10.0 and the library are usable."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        lib = _lib.load()
+    except _lib.NativeLibraryError:
+        return False
+    return bool(lib.mxfa_is_available())
+
+
+def _bf16(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return 1
+    if t.dtype == torch.float16:
+        return 0
+    raise TypeError(f"the CUDA backend supports float16 and bfloat16, got {t.dtype}")
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    return t if (t.dtype == torch.int32 and t.is_contiguous()) else t.to(torch.int32).contiguous()
+
+
+def _contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+# ------------------------------------------------------------------ prefill
+
+def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
+                           softmax_scale, *, return_lse: bool = False):
+    """Packed varlen forward: q [Tq, HQ, D], k/v [Tk, HKV, D] -> out [Tq, HQ, D]."""
+    q, k, v = _contig(q), _contig(k), _contig(v)
+    out = torch.empty_like(q)
+    lse = torch.empty((q.shape[0], q.shape[1]), device=q.device, dtype=torch.float32) if return_lse else None
+    cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
+    batch = cu_q.numel() - 1
+    with torch.cuda.device(q.device):
+        rc = _lib.load().mxfa_varlen_fwd_launch(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_q.data_ptr(), cu_k.data_ptr(), out.data_ptr(),
+            _lib.ptr(lse), batch, int(max_seqlen_q), int(max_seqlen_k), q.shape[1], k.shape[1], q.shape[2],
+            int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
+    _lib.check(rc, "mxfa_varlen_fwd_launch")
+    return (out, lse) if return_lse else out
+
+
+def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False):
+    """Dense batched forward: q [B, Sq, HQ, D], k/v [B, Sk, HKV, D] -> out [B, Sq, HQ, D]."""
+    q, k, v = _contig(q), _contig(k), _contig(v)
+    out = torch.empty_like(q)
+    B, Sq, HQ, D = q.shape
+    lse = torch.empty((B, Sq, HQ), device=q.device, dtype=torch.float32) if return_lse else None
+    with torch.cuda.device(q.device):
+        rc = _lib.load().mxfa_varlen_fwd_launch(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None, out.data_ptr(), _lib.ptr(lse), B, Sq,
+            k.shape[1], HQ, k.shape[2], D, int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
+    _lib.check(rc, "mxfa_varlen_fwd_launch")
+    return (out, lse) if return_lse else out
+
+
+# ------------------------------------------------------------------ decode
+
+def kvcache_plan(batch: int, q_len: int, q_heads: int, kv_heads: int, head_dim: int, max_len: int):
+    """(num_splits, chunk_len) the library picks for this shape on the current device."""
+    import ctypes
+
+    np_, cl = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().mxfa_kvcache_plan(batch, q_len, q_heads, kv_heads, head_dim, max_len,
+                                              ctypes.byref(np_), ctypes.byref(cl)), "mxfa_kvcache_plan")
+    return int(np_.value), int(cl.value)
+
+
+def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
+                      append_len: int = 0, return_lse: bool = False, num_splits: int = 0, chunk_len: int = 0,
+                      out=None):
+    """Attention of q [B, Sq, HQ, D] over the cached tokens (+ ``append_len``).
+
+    ``cache_seqlens`` holds the lengths before the append; nothing is written
+    to the caches here.  ``num_splits``/``chunk_len`` 0 = library plan.
+    """
+    B, Sq, HQ, D = q.shape
+    q = _contig(q)
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("the CUDA backend requires contiguous k_cache / v_cache")
+    seq = _i32(cache_seqlens)
+    bt = None if block_table is None else _i32(block_table)
+    PS = k_cache.shape[1]
+    HKV = k_cache.shape[2]
+    if bt is not None:
+        btw, pages = bt.shape[1], k_cache.shape[0]
+        max_len = btw * PS
+    else:
+        btw, pages = 0, k_cache.shape[0]
+        max_len = PS
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty((B, Sq, HQ), device=q.device, dtype=torch.float32) if return_lse else None
+    lib = _lib.load()
+    if num_splits <= 0 or chunk_len <= 0:
+        num_splits, chunk_len = kvcache_plan(B, Sq, HQ, HKV, D, max_len)
+    ws = None
+    ws_bytes = 0
+    if num_splits > 1:
+        ws_bytes = int(lib.mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits))
+        ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        rc = lib.mxfa_kvcache_attention_launch(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), out.data_ptr(),
+            _lib.ptr(lse), _lib.ptr(ws), ws_bytes, B, Sq, HQ, HKV, D, PS, btw, pages, int(append_len),
+            num_splits, chunk_len, int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
+    _lib.check(rc, "mxfa_kvcache_attention_launch")
+    return (out, lse) if return_lse else out
+
+
+def kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table) -> None:
+    """Write k/v [B, Sk, HKV, D] at positions cache_seqlens[b] + i (no length update)."""
+    k, v = _contig(k), _contig(v)
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("the CUDA backend requires contiguous k_cache / v_cache")
+    seq = _i32(cache_seqlens)
+    bt = None if block_table is None else _i32(block_table)
+    B, Sk, HKV, D = k.shape
+    with torch.cuda.device(k.device):
+        rc = _lib.load().mxfa_kv_append_launch(
+            k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), B,
+            Sk, HKV, D, k_cache.shape[1], 0 if bt is None else bt.shape[1], k_cache.shape[0], k.element_size(),
+            _stream(k))
+    _lib.check(rc, "mxfa_kv_append_launch")
+
+
+def seqlens_add_(cache_seqlens: torch.Tensor, delta: int) -> None:
+    """In-place ``cache_seqlens += delta`` on the device (int32 or int64)."""
+    if cache_seqlens.dtype not in (torch.int32, torch.int64) or not cache_seqlens.is_contiguous():
+        cache_seqlens.add_(delta)
+        return
+    with torch.cuda.device(cache_seqlens.device):
+        rc = _lib.load().mxfa_seqlens_add_launch(
+            cache_seqlens.data_ptr(), int(cache_seqlens.dtype == torch.int64), cache_seqlens.numel(), int(delta),
+            _stream(cache_seqlens))
+    _lib.check(rc, "mxfa_seqlens_add_launch")
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, softmax_scale, causal):
+    """``flash_attn_with_kvcache`` semantics of the reference (reference.py:88-139).
+
+    Appends ``k``/``v`` (when given) at the current lengths, attends over the
+    grown cache, then advances ``cache_seqlens`` in place -- all on the
+    current stream, with no host synchronisation.
+    """
+    if q.shape[1] == 0:
+        if k is not None:
+            kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
+            seqlens_add_(cache_seqlens, k.shape[1])
+        return torch.empty_like(q)
+    append_len = 0
+    if k is not None:
+        kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
+        append_len = k.shape[1]
+    out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
+                            append_len=append_len)
+    if k is not None:
+        seqlens_add_(cache_seqlens, append_len)
+    return out
+
+
+# ------------------------------------------------------ combine / merge
+
+def split_combine(ows, mdws, rows: int, head_dim: int, num_splits: int, dtype, *, lse: bool = False,
+                  out=None):
+    """LSE-merge split partials ows [rows, NP, D], mdws [rows, NP, 2] -> out [rows, D]."""
+    if out is None:
+        out = torch.empty((rows, head_dim), device=ows.device, dtype=dtype)
+    lse_t = torch.empty((rows,), device=ows.device, dtype=torch.float32) if lse else None
+    with torch.cuda.device(ows.device):
+        rc = _lib.load().mxfa_split_combine_launch(
+            ows.data_ptr(), mdws.data_ptr(), out.data_ptr(), None, _lib.ptr(lse_t), rows, head_dim, num_splits,
+            int(dtype == torch.bfloat16), _stream(ows))
+    _lib.check(rc, "mxfa_split_combine_launch")
+    return (out, lse_t) if lse else out
+
+
+def lse_merge(packed, rows: int, head_dim: int, dtype, *, lse: bool = False, out=None):
+    """Merge per-rank (O, LSE): packed f32 [N, rows, D + 1] -> out [rows, D] (and LSE)."""
+    n_ranks = packed.shape[0]
+    if out is None:
+        out = torch.empty((rows, head_dim), device=packed.device, dtype=dtype)
+    lse_t = torch.empty((rows,), device=packed.device, dtype=torch.float32) if lse else None
+    with torch.cuda.device(packed.device):
+        rc = _lib.load().mxfa_lse_merge_launch(
+            packed.data_ptr(), out.data_ptr(), _lib.ptr(lse_t), n_ranks, rows, head_dim,
+            int(dtype == torch.bfloat16), _stream(packed))
+    _lib.check(rc, "mxfa_lse_merge_launch")
+    return (out, lse_t) if lse else out

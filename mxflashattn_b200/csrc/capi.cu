@@ -1,0 +1,436 @@
+// capi.cu -- extern "C" entry points of libmxfa_b200.so (see include/mxfa_b200.h).
+//
+// Host-side responsibilities only: argument guards with the reference's
+// return codes, the split plan, TMA tensor-map encoding (through the driver
+// entry point, so the library needs no libcuda link), per-device kernel
+// attributes, and stream-ordered launches.  No entry point synchronises or
+// reads device memory on the host except mxfa_read_error_flags.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "decode.cuh"
+#include "prefill_mma.cuh"
+
+namespace mxfa {
+
+namespace {
+
+thread_local char g_last_error[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return MXFA_OK;
+}
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int sm_count() {
+  static std::atomic<int> cache[64];
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64) {
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Opt a kernel into > 48 KB dynamic shared memory once per device.
+template <typename K>
+int ensure_smem(K kernel, int bytes, std::atomic<unsigned long long>& done) {
+  const int dev = current_device();
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return MXFA_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return MXFA_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D map over a KV cache viewed as [slots = P*PS][HKV][D] with a
+// (64 columns, 1 head, 16 slots) box and 128-byte swizzle.
+bool encode_kv_map(CUtensorMap* map, const void* base, int D, int HKV, long long slots) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  if (slots <= 0 || slots > 0xFFFFFFFFll) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(HKV), static_cast<cuuint64_t>(slots)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(HKV) * D * 2};
+  cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kTileTok)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------ decode
+
+template <typename T, int HD, int NT, bool kTma>
+int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv,
+                       cudaStream_t st) {
+  static std::atomic<unsigned long long> done{0};
+  auto kern = paged_decode_kernel<T, HD, NT, kTma>;
+  const int smem = DecodeCfg<HD>::kSmemBytes;
+  if (int rc = ensure_smem(kern, smem, done)) return rc;
+  kern<<<grid, kDecThreads, smem, st>>>(p, tk, tv);
+  return check_launch("paged_decode_kernel");
+}
+
+template <typename T, int HD>
+int launch_decode_t(const DecodeParams& p, int nt, bool tma, dim3 grid, const CUtensorMap& tk,
+                    const CUtensorMap& tv, cudaStream_t st) {
+  if (nt == 1)
+    return tma ? launch_decode_inst<T, HD, 1, true>(p, grid, tk, tv, st)
+               : launch_decode_inst<T, HD, 1, false>(p, grid, tk, tv, st);
+  return tma ? launch_decode_inst<T, HD, 2, true>(p, grid, tk, tv, st)
+             : launch_decode_inst<T, HD, 2, false>(p, grid, tk, tv, st);
+}
+
+// Runs the decode kernel (split or direct) for a validated configuration.
+int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
+  const int rows_kv = p.Sq * p.GQ;
+  const int nt = rows_kv <= 8 ? 1 : 2;
+  const int row_groups = (rows_kv + 8 * nt - 1) / (8 * nt);
+  if (static_cast<long long>(p.HKV) * row_groups > 65535)
+    return fail(MXFA_ERR_UNSUPPORTED, "too many KV heads x query-row groups (%d x %d)", p.HKV, row_groups);
+  const int nz = p.ows != nullptr ? p.NP : 1;
+  if (nz > 65535) return fail(MXFA_ERR_UNSUPPORTED, "too many splits (%d)", nz);
+  dim3 grid(p.B, p.HKV * row_groups, nz);
+  CUtensorMap tk, tv;
+  std::memset(&tk, 0, sizeof(tk));
+  std::memset(&tv, 0, sizeof(tv));
+  bool tma = (p.PS % kTileTok) == 0;
+  if (tma) {
+    const long long slots = static_cast<long long>(p.P) * p.PS;
+    tma = encode_kv_map(&tk, p.k, D, p.HKV, slots) && encode_kv_map(&tv, p.v, D, p.HKV, slots);
+  }
+  if (bf16)
+    return D == 128 ? launch_decode_t<__nv_bfloat16, 128>(p, nt, tma, grid, tk, tv, st)
+                    : launch_decode_t<__nv_bfloat16, 64>(p, nt, tma, grid, tk, tv, st);
+  return D == 128 ? launch_decode_t<__half, 128>(p, nt, tma, grid, tk, tv, st)
+                  : launch_decode_t<__half, 64>(p, nt, tma, grid, tk, tv, st);
+}
+
+template <typename T, int HD, bool kPacked>
+int launch_combine_inst(const float* ows, const float* mdws, void* out, float* out_f32, float* lse, int rows,
+                        int NP, cudaStream_t st) {
+  split_combine_kernel<T, HD, kPacked>
+      <<<(rows + 3) / 4, 128, 0, st>>>(ows, mdws, static_cast<T*>(out), out_f32, lse, rows, NP);
+  return check_launch("split_combine_kernel");
+}
+
+template <bool kPacked>
+int run_combine(const float* ows, const float* mdws, void* out, float* out_f32, float* lse, int rows, int D,
+                int NP, bool bf16, cudaStream_t st) {
+  if (rows == 0) return MXFA_OK;
+  if (bf16)
+    return D == 128 ? launch_combine_inst<__nv_bfloat16, 128, kPacked>(ows, mdws, out, out_f32, lse, rows, NP, st)
+                    : launch_combine_inst<__nv_bfloat16, 64, kPacked>(ows, mdws, out, out_f32, lse, rows, NP, st);
+  return D == 128 ? launch_combine_inst<__half, 128, kPacked>(ows, mdws, out, out_f32, lse, rows, NP, st)
+                  : launch_combine_inst<__half, 64, kPacked>(ows, mdws, out, out_f32, lse, rows, NP, st);
+}
+
+// Split plan: enough CTAs to fill every SM twice, chunks of >= 256 positions.
+void plan_splits(int B, int HKV, int row_groups, int max_len, int* np_out, int* clen_out) {
+  const long long units = static_cast<long long>(B) * HKV * row_groups;
+  const long long target = 2LL * sm_count();
+  int np = 1;
+  if (units > 0 && units < target && max_len > 256) {
+    np = static_cast<int>((target + units - 1) / units);
+    const int cap = (max_len + 255) / 256;
+    if (np > cap) np = cap;
+    if (np > 1024) np = 1024;
+  }
+  if (np < 1) np = 1;
+  int clen = (max_len + np - 1) / np;
+  clen = ((clen + kTileTok - 1) / kTileTok) * kTileTok;
+  if (clen < kTileTok) clen = kTileTok;
+  np = (max_len + clen - 1) / clen;
+  if (np < 1) np = 1;
+  *np_out = np;
+  *clen_out = clen;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace mxfa
+
+using namespace mxfa;
+
+extern "C" {
+
+int mxfa_abi_version(void) { return 1; }
+
+const char* mxfa_last_error(void) { return g_last_error; }
+
+int mxfa_is_available(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  cudaGetLastError();
+  return (major == 10 && minor == 0) ? 1 : 0;
+}
+
+int mxfa_read_error_flags(unsigned int* flags) {
+  if (flags == nullptr) return fail(MXFA_ERR_INVALID, "flags is NULL");
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_error_flags, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_error_flags, &zero, sizeof(zero));
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "reading error flags failed: %s", cudaGetErrorString(e));
+  *flags = v;
+  return MXFA_OK;
+}
+
+size_t mxfa_split_workspace_bytes(int rows, int D, int NP) {
+  if (rows <= 0 || D <= 0 || NP <= 0) return 0;
+  return static_cast<size_t>(rows) * NP * (static_cast<size_t>(D) + 2) * sizeof(float);
+}
+
+int mxfa_kvcache_plan(int B, int Sq, int HQ, int HKV, int D, int max_len, int* num_splits, int* chunk_len) {
+  if (num_splits == nullptr || chunk_len == nullptr) return fail(MXFA_ERR_INVALID, "null output pointer");
+  if (B <= 0 || Sq <= 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0 || max_len < 0)
+    return fail(MXFA_ERR_INVALID, "invalid plan arguments");
+  (void)D;
+  const int rows_kv = Sq * (HQ / HKV);
+  const int nt = rows_kv <= 8 ? 1 : 2;
+  const int row_groups = (rows_kv + 8 * nt - 1) / (8 * nt);
+  plan_splits(B, HKV, row_groups, max_len < 1 ? 1 : max_len, num_splits, chunk_len);
+  return MXFA_OK;
+}
+
+int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
+                                  void* workspace, size_t workspace_bytes, int B, int Sq, int HQ, int HKV, int D,
+                                  int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
+                                  int causal, int bf16, float scale, void* stream) {
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
+    return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
+  if (B == 0 || Sq == 0) return MXFA_OK;
+  if (PS <= 0 || num_pages <= 0 || append_len < 0) return fail(MXFA_ERR_INVALID, "bad cache geometry");
+  if (block_table != nullptr && BTW <= 0) return fail(MXFA_ERR_INVALID, "block table width must be positive");
+  if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned (out 8-byte)");
+  DecodeParams p{};
+  p.q = q;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.bt = block_table;
+  p.seqlens = seqlens;
+  p.out = out;
+  p.lse = lse;
+  p.B = B;
+  p.Sq = Sq;
+  p.HQ = HQ;
+  p.HKV = HKV;
+  p.PS = PS;
+  p.BTW = block_table ? BTW : 1;
+  p.P = num_pages;
+  p.GQ = HQ / HKV;
+  p.append_len = append_len;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * kLog2e;
+  const int max_len = block_table ? BTW * PS : PS;
+  if (num_splits <= 0 || chunk_len <= 0) {
+    mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (num_splits <= 1) {
+    p.NP = 1;
+    p.c_len = max_len;
+    return run_decode(p, D, bf16 != 0, st);
+  }
+  const long long rows = static_cast<long long>(B) * Sq * HQ;
+  const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
+  p.NP = num_splits;
+  p.c_len = chunk_len;
+  p.ows = static_cast<float*>(workspace);
+  p.mdws = p.ows + rows * num_splits * D;
+  if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
+  return run_combine<false>(p.ows, p.mdws, out, nullptr, lse, static_cast<int>(rows), D, num_splits, bf16 != 0, st);
+}
+
+int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt, const void* sl,
+                                   void* out, void* ows, void* mdws, float scale, int B, int HQ, int HKV, int D,
+                                   int PS, int BTW, int bf16, int NP, int c_len, int um, void* stream) {
+  // guards of m1_kernel.cpp:1212-1215
+  if (HKV <= 0 || HQ % HKV != 0) return fail(MXFA_ERR_UNSUPPORTED, "HQ %% HKV != 0");
+  if (D != 128 && D != 64) return fail(MXFA_ERR_UNSUPPORTED, "split kernel unsupported config: D=%d", D);
+  const int GQ = HQ / HKV;
+  if ((GQ != 2 && GQ != 4 && GQ != 8) || NP < 1)
+    return fail(MXFA_ERR_UNSUPPORTED, "split kernel unsupported config: D=%d GQ=%d NP=%d", D, GQ, NP);
+  (void)um;  // every softmax variant is served by the same online softmax
+  if (B <= 0) return MXFA_OK;
+  if (!q || !k || !v || !bt || !sl || !out || !ows || !mdws || PS <= 0 || BTW <= 0 || c_len <= 0)
+    return fail(MXFA_ERR_INVALID, "invalid split-decode argument");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(ows) || (reinterpret_cast<uintptr_t>(mdws) & 7))
+    return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
+  DecodeParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.bt = static_cast<const int*>(bt);
+  p.seqlens = static_cast<const int*>(sl);
+  p.out = out;
+  p.ows = static_cast<float*>(ows);
+  p.mdws = static_cast<float*>(mdws);
+  p.B = B;
+  p.Sq = 1;
+  p.HQ = HQ;
+  p.HKV = HKV;
+  p.PS = PS;
+  p.BTW = BTW;
+  // the reference ABI carries no page count: bound the addressable slots only
+  p.P = static_cast<int>(0x7FFFFFFFll / PS);
+  p.GQ = GQ;
+  p.NP = NP;
+  p.c_len = c_len;
+  p.scale_log2 = scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
+  return run_combine<false>(p.ows, p.mdws, out, nullptr, nullptr, B * HQ, D, NP, bf16 != 0, st);
+}
+
+int mxfa_split_combine_launch(const float* ows, const float* mdws, void* out, float* out_f32, float* lse, int rows,
+                              int D, int NP, int bf16, void* stream) {
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (rows < 0 || NP < 1 || !ows || !mdws) return fail(MXFA_ERR_INVALID, "invalid combine argument");
+  if (!aligned16(ows)) return fail(MXFA_ERR_INVALID, "ows must be 16-byte aligned");
+  return run_combine<false>(ows, mdws, out, out_f32, lse, rows, D, NP, bf16 != 0,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int mxfa_lse_merge_launch(const float* packed, void* out, float* lse, int N, int rows, int D, int bf16,
+                          void* stream) {
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (rows < 0 || N < 1 || !packed || !out) return fail(MXFA_ERR_INVALID, "invalid merge argument");
+  return run_combine<true>(packed, nullptr, out, nullptr, lse, rows, D, N, bf16 != 0,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int mxfa_kv_append_launch(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                          const int32_t* block_table, const int32_t* seqlens, int B, int Sk, int HKV, int D, int PS,
+                          int BTW, int num_pages, int elem_bytes, void* stream) {
+  if (B < 0 || Sk < 0 || HKV <= 0 || D <= 0 || PS <= 0 || num_pages <= 0 || elem_bytes <= 0)
+    return fail(MXFA_ERR_INVALID, "invalid append geometry");
+  if (B == 0 || Sk == 0) return MXFA_OK;
+  if (!k_new || !v_new || !k_cache || !v_cache || !seqlens) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  const int row_bytes = D * elem_bytes;
+  if (row_bytes % 16 != 0 || !aligned16(k_new) || !aligned16(v_new) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(MXFA_ERR_INVALID, "append rows must be 16-byte multiples on 16-byte aligned tensors");
+  if (block_table != nullptr && BTW <= 0) return fail(MXFA_ERR_INVALID, "block table width must be positive");
+  AppendParams p{};
+  p.k_new = static_cast<const uint8_t*>(k_new);
+  p.v_new = static_cast<const uint8_t*>(v_new);
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.bt = block_table;
+  p.seqlens = seqlens;
+  p.B = B;
+  p.Sk = Sk;
+  p.HKV = HKV;
+  p.row_bytes = row_bytes;
+  p.PS = PS;
+  p.BTW = block_table ? BTW : 1;
+  p.P = num_pages;
+  const long long total = static_cast<long long>(B) * Sk * HKV * (row_bytes / 16);
+  long long blocks = (total + 255) / 256;
+  if (blocks > 8LL * sm_count()) blocks = 8LL * sm_count();
+  kv_append_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("kv_append_kernel");
+}
+
+int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void* stream) {
+  if (B < 0 || (B > 0 && seqlens == nullptr)) return fail(MXFA_ERR_INVALID, "invalid seqlens argument");
+  if (B == 0 || delta == 0) return MXFA_OK;
+  seqlens_add_kernel<<<(B + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(seqlens, is_int64, B, delta);
+  return check_launch("seqlens_add_kernel");
+}
+
+int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                           void* out, float* lse, int B, int max_q, int max_k, int HQ, int HKV, int D, int causal,
+                           int bf16, float scale, void* stream) {
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (B < 0 || max_q < 0 || max_k < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
+    return fail(MXFA_ERR_INVALID, "bad varlen geometry");
+  if ((cu_q == nullptr) != (cu_k == nullptr)) return fail(MXFA_ERR_INVALID, "cu_q and cu_k must both be given");
+  if (B == 0 || max_q == 0) return MXFA_OK;
+  if (!q || !k || !v || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (HQ > 65535 || B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "grid too large");
+  PrefillParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
+  p.out = out;
+  p.lse = lse;
+  p.B = B;
+  p.Sq = max_q;
+  p.Sk = max_k;
+  p.HQ = HQ;
+  p.HKV = HKV;
+  p.GQ = HQ / HKV;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * kLog2e;
+  dim3 grid((max_q + kPfRows - 1) / kPfRows, HQ, B);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done) -> int {
+    if (int rc = ensure_smem(kern, smem, done)) return rc;
+    kern<<<grid, kPfThreads, smem, st>>>(p);
+    return check_launch("prefill_mma_kernel");
+  };
+  static std::atomic<unsigned long long> d0{0}, d1{0}, d2{0}, d3{0};
+  if (bf16)
+    return D == 128 ? go(prefill_mma_kernel<__nv_bfloat16, 128>, PrefillCfg<128>::kSmemBytes, d0)
+                    : go(prefill_mma_kernel<__nv_bfloat16, 64>, PrefillCfg<64>::kSmemBytes, d1);
+  return D == 128 ? go(prefill_mma_kernel<__half, 128>, PrefillCfg<128>::kSmemBytes, d2)
+                  : go(prefill_mma_kernel<__half, 64>, PrefillCfg<64>::kSmemBytes, d3);
+}
+
+}  // extern "C"

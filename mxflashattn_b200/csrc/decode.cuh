@@ -1,0 +1,557 @@
+// decode.cuh -- split-KV paged decode attention for sm_100a.
+//
+// One CTA per (sequence b, KV head, query-row group, split z).  All query
+// rows that share the KV head (GQ heads x Sq query positions, up to 16 per
+// group) are packed into the N dimension of a swapped tensor-core product,
+// so every paged K/V row is read from HBM once per CTA:
+//
+//   S^T[16 tok, 8 rows] = K[16 tok, D] . Q^T[D, 8 rows]          (m16n8k16)
+//   O^T[D, 8 rows]     += V^T[D, 16 tok] . P[16 tok, 8 rows]       (m16n8k16)
+//
+// Warp 4 is the producer: it resolves the block table and streams 16-token
+// tiles of K and V into a ring of shared-memory slots -- one TMA box per
+// 64-column block when the page size is a multiple of 16, cp.async row
+// gathers otherwise -- and each slot's mbarrier counts the bytes in.  Warps
+// 0-3 consume tiles round-robin, run an online softmax in the log2 domain
+// (row max by warp shuffles across the 8 token groups), and merge their
+// (m, l, O) states through shared memory at the end.  A split writes the
+// unnormalised partial state (o, m, d) for the combine kernel; a single-split
+// launch writes the normalised output (and LSE) directly.
+//
+// Reference behaviour followed: the split geometry and partial-state
+// contract of paged_decode_v3 / split_combine (csrc_native/m1_kernel.cpp:
+// 563-577, 846-853, 862-888); the attention math of mxflashattn/reference.py.
+#pragma once
+
+#include "common.cuh"
+
+namespace mxfa {
+
+struct DecodeParams {
+  const void* q;         // [B, Sq, HQ, D]
+  const void* k;         // paged [P, PS, HKV, D] or dense [B, PS, HKV, D]
+  const void* v;
+  const int* bt;         // [B, BTW] or nullptr (dense: page of batch b is b)
+  const int* seqlens;    // [B] cached length before this call
+  void* out;             // direct mode: [B, Sq, HQ, D]
+  float* lse;            // direct mode, optional: [B, Sq, HQ]
+  float* ows;            // split mode when non-null: [rows, NP, D] (rows = B*Sq*HQ)
+  float* mdws;           // split mode: [rows, NP, 2]
+  int B, Sq, HQ, HKV, PS, BTW, P;
+  int GQ;                // HQ / HKV
+  int append_len;        // total length = seqlens[b] + append_len
+  int NP, c_len;         // splits; chunk z covers [z*c_len, (z+1)*c_len)
+  int causal;
+  float scale_log2;      // softmax_scale * log2(e)
+};
+
+constexpr int kDecConsumerWarps = 4;
+constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
+constexpr int kTileTok = 16;
+
+template <int HD>
+struct DecodeCfg {
+  static constexpr int kDBlk = HD / 64;                  // 128-byte column blocks per row
+  static constexpr int kBlkBytes = kTileTok * 128;       // one column block of one tile: 2 KB
+  static constexpr int kTileBytes = kTileTok * HD * 2;   // K (or V) bytes of one tile
+  static constexpr int kSlotBytes = 2 * kTileBytes;      // K + V
+  static constexpr int kSlots = (HD == 128) ? 12 : 24;   // 96 KB ring either way
+  static constexpr int kRingBytes = kSlots * kSlotBytes;
+  static constexpr int kSmemBytes = kRingBytes + 2 * kSlots * 8 + 1024;
+};
+
+// Merge scratch laid over the ring once all tiles are consumed.
+template <int HD, int NT>
+struct DecodeMerge {
+  static constexpr int kCols = 8 * NT;
+  static constexpr int kStride = HD + 4;  // padded row: conflict-free fragment stores
+  static constexpr int kOBytes = kDecConsumerWarps * kCols * kStride * 4;
+  static constexpr int kBytes = kOBytes + 2 * kDecConsumerWarps * kCols * 4;
+};
+
+template <typename T, int HD, int NT, bool kTma>
+__global__ void __launch_bounds__(kDecThreads, 2)
+    paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv) {
+  using Cfg = DecodeCfg<HD>;
+  static_assert(DecodeMerge<HD, NT>::kBytes <= Cfg::kRingBytes, "merge scratch must fit the ring");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + Cfg::kRingBytes);
+  uint64_t* empty = full + Cfg::kSlots;
+
+  const int b = blockIdx.x;
+  const int kvh = blockIdx.y % p.HKV;
+  const int rg = blockIdx.y / p.HKV;
+  const int z = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int total_len = p.seqlens[b] + p.append_len;
+  // split mode (partials written for a combine) whenever a workspace is given;
+  // chunk z then covers [z*c_len, (z+1)*c_len) exactly as the reference's split
+  int lo = 0, hi = total_len;
+  if (p.ows != nullptr) {
+    lo = z * p.c_len;
+    hi = min(lo + p.c_len, total_len);
+  }
+  const int tile0 = (lo / kTileTok) * kTileTok;
+  const int ntiles = (hi > lo) ? (hi - tile0 + kTileTok - 1) / kTileTok : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kSlots; ++s) {
+      mbar_init(&full[s], kTma ? 1 : 32);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- producer
+  if (warp == kDecConsumerWarps) {
+    const T* kc = static_cast<const T*>(p.k);
+    const T* vc = static_cast<const T*>(p.v);
+    if constexpr (kTma) {
+      if (lane == 0) {
+        prefetch_tensormap(&tmk);
+        prefetch_tensormap(&tmv);
+      }
+      int abort = 0;
+      for (int base = 0; base < ntiles && !abort; base += 32) {
+        // lane j resolves the physical slot row of tile base + j (one load per lane)
+        const int t = base + lane;
+        int slot_row = 0;
+        if (t < ntiles) {
+          const int pos = tile0 + t * kTileTok;
+          int page = pos / p.PS;
+          int phys = b;
+          if (p.bt != nullptr) {
+            if (page >= p.BTW) {
+              raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+              page = p.BTW - 1;
+            }
+            phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+          }
+          if (phys < 0 || phys >= p.P) {
+            raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+            phys = p.P;  // box lies past the tensor: TMA fills zeros, reads nothing
+          }
+          slot_row = phys * p.PS + (pos % p.PS);
+        }
+        const int n = min(32, ntiles - base);
+        for (int j = 0; j < n; ++j) {
+          const int row = __shfl_sync(0xffffffffu, slot_row, j);
+          if (lane == 0 && !abort) {
+            const int tt = base + j;
+            const int slot = tt % Cfg::kSlots;
+            const int use = tt / Cfg::kSlots;
+            if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
+              abort = 1;
+            } else {
+              mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kTileBytes);
+              uint8_t* kd = ring + slot * Cfg::kSlotBytes;
+              uint8_t* vd = kd + Cfg::kTileBytes;
+#pragma unroll
+              for (int db = 0; db < Cfg::kDBlk; ++db) {
+                tma_load_3d(kd + db * Cfg::kBlkBytes, &tmk, &full[slot], db * 64, kvh, row);
+                tma_load_3d(vd + db * Cfg::kBlkBytes, &tmv, &full[slot], db * 64, kvh, row);
+              }
+            }
+          }
+          abort = __shfl_sync(0xffffffffu, abort, 0);
+          if (abort) break;
+        }
+      }
+    } else {
+      constexpr int kChunks = kTileTok * (HD / 8);  // 16-byte chunks per tile per tensor
+      for (int t = 0; t < ntiles; ++t) {
+        const int slot = t % Cfg::kSlots;
+        const int use = t / Cfg::kSlots;
+        if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) break;
+        uint8_t* kd = ring + slot * Cfg::kSlotBytes;
+        uint8_t* vd = kd + Cfg::kTileBytes;
+        const int pos0 = tile0 + t * kTileTok;
+#pragma unroll 2
+        for (int c = lane; c < kChunks; c += 32) {
+          const int r = c / (HD / 8);
+          const int ch = c % (HD / 8);
+          const int pos = pos0 + r;
+          if (pos < lo || pos >= hi) continue;  // left stale; consumers mask / zero it
+          const int page = pos / p.PS;
+          int phys = b;
+          if (p.bt != nullptr) {
+            if (page >= p.BTW) {
+              raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+              continue;
+            }
+            phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+          }
+          if (phys < 0 || phys >= p.P) {
+            raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+            continue;
+          }
+          const size_t off =
+              ((static_cast<size_t>(phys) * p.PS + (pos % p.PS)) * p.HKV + kvh) * HD + ch * 8;
+          const uint32_t so = (ch >> 3) * Cfg::kBlkBytes + swz128(r, ch & 7);
+          cp_async_16(kd + so, kc + off);
+          cp_async_16(vd + so, vc + off);
+        }
+        cp_async_mbar_arrive_noinc(&full[slot]);
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int g = lane >> 2;
+  const int t4 = lane & 3;
+  const int rows_total = p.Sq * p.GQ;
+  const int row_base = rg * 8 * NT;
+  const T* qptr = static_cast<const T*>(p.q);
+
+  // Q^T fragments (B operand): thread holds Q[row g][d = kk*16 + 2*t4 + {0,1}, +8]
+  uint32_t qf[HD / 16][NT][2];
+  int lim[NT][2];  // last visible key position of the two rows this thread owns in each n-tile
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int row = row_base + nt * 8 + g;
+    const T* qr = nullptr;
+    if (row < rows_total) {
+      const int i = row / p.GQ;
+      const int h = kvh * p.GQ + row % p.GQ;
+      qr = qptr + (static_cast<size_t>(b * p.Sq + i) * p.HQ + h) * HD;
+    }
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      qf[kk][nt][0] = qr ? ld_u32(qr + kk * 16 + 2 * t4) : 0u;
+      qf[kk][nt][1] = qr ? ld_u32(qr + kk * 16 + 8 + 2 * t4) : 0u;
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int col_row = row_base + nt * 8 + 2 * t4 + c;
+      if (col_row >= rows_total)
+        lim[nt][c] = -1;
+      else if (p.causal)
+        lim[nt][c] = total_len - p.Sq + col_row / p.GQ;
+      else
+        lim[nt][c] = 0x7fffffff;
+    }
+  }
+
+  float m[NT][2], l[NT][2];
+  float o[HD / 16][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = -INFINITY;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int mi = 0; mi < HD / 16; ++mi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mi][nt][e] = 0.f;
+  }
+
+  for (int t = warp; t < ntiles; t += kDecConsumerWarps) {
+    const int slot = t % Cfg::kSlots;
+    if (!mbar_wait(&full[slot], (t / Cfg::kSlots) & 1)) break;
+    uint8_t* kd = ring + slot * Cfg::kSlotBytes;
+    uint8_t* vd = kd + Cfg::kTileBytes;
+    const int pos0 = tile0 + t * kTileTok;
+    const bool partial = (pos0 < lo) || (pos0 + kTileTok > hi);
+    if (partial) {
+      // rows outside [lo, hi) may hold padding (even NaN): zero their V so p=0 rows add nothing
+      for (int c = lane; c < kTileTok * (HD / 8); c += 32) {
+        const int r = c / (HD / 8);
+        const int ch = c % (HD / 8);
+        const int pos = pos0 + r;
+        if (pos < lo || pos >= hi)
+          *reinterpret_cast<uint4*>(vd + (ch >> 3) * Cfg::kBlkBytes + swz128(r, ch & 7)) =
+              make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+    const uint32_t kbase = smem_u32(kd);
+    const uint32_t vbase = smem_u32(vd);
+
+    float s[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    {
+      const int q8 = lane >> 3;
+      const int r = ((q8 & 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const int dch = kk * 2 + (q8 >> 1);  // 8-element chunk index along D
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kbase + (dch >> 3) * Cfg::kBlkBytes + swz128(r, dch & 7), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Elem<T>::mma(s[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
+      }
+    }
+
+    // mask + scale into the log2 domain
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int pos = pos0 + g + ((e >> 1) << 3);
+        const bool ok = pos >= lo && pos < hi && pos <= lim[nt][e & 1];
+        s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
+      }
+
+    // online softmax per query row (a column of S^T)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float mx = fmaxf(s[nt][c], s[nt][c + 2]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m[nt][c], mx);
+        float alpha = 1.f, p0 = 0.f, p1 = 0.f;
+        if (m_new != -INFINITY) {
+          alpha = fast_exp2(m[nt][c] - m_new);
+          p0 = fast_exp2(s[nt][c] - m_new);
+          p1 = fast_exp2(s[nt][c + 2] - m_new);
+        }
+        l[nt][c] = l[nt][c] * alpha + p0 + p1;
+        m[nt][c] = m_new;
+        s[nt][c] = p0;
+        s[nt][c + 2] = p1;
+#pragma unroll
+        for (int mi = 0; mi < HD / 16; ++mi) {
+          o[mi][nt][c] *= alpha;
+          o[mi][nt][c + 2] *= alpha;
+        }
+      }
+
+    // P (tok x rows) -> B fragments of the PV product
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      pb[nt][0] = movmatrix_trans(Elem<T>::pack(s[nt][0], s[nt][1]));
+      pb[nt][1] = movmatrix_trans(Elem<T>::pack(s[nt][2], s[nt][3]));
+    }
+    {
+      const int q8 = lane >> 3;
+      const int r = ((q8 >> 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int mi = 0; mi < HD / 16; ++mi) {
+        const int dch = mi * 2 + (q8 & 1);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(vbase + (dch >> 3) * Cfg::kBlkBytes + swz128(r, dch & 7), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+      }
+    }
+    __syncwarp();
+    if (partial) fence_proxy_async_smem();  // generic zero-stores before the next TMA write
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+
+  // row sums: reduce over the 8 token groups
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      l[nt][c] += __shfl_xor_sync(0xffffffffu, l[nt][c], 4);
+      l[nt][c] += __shfl_xor_sync(0xffffffffu, l[nt][c], 8);
+      l[nt][c] += __shfl_xor_sync(0xffffffffu, l[nt][c], 16);
+    }
+
+  // ---------------------------------------------------- merge the 4 warps
+  using Mg = DecodeMerge<HD, NT>;
+  named_barrier_sync(1, kDecConsumerWarps * 32);  // every consumer finished reading the ring
+  float* om = reinterpret_cast<float*>(ring);
+  float* mm = reinterpret_cast<float*>(ring + Mg::kOBytes);
+  float* lm = mm + kDecConsumerWarps * Mg::kCols;
+#pragma unroll
+  for (int mi = 0; mi < HD / 16; ++mi)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = nt * 8 + 2 * t4 + (e & 1);
+        const int d = mi * 16 + g + ((e >> 1) << 3);
+        om[(warp * Mg::kCols + col) * Mg::kStride + d] = o[mi][nt][e];
+      }
+  if (g == 0) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int col = nt * 8 + 2 * t4 + c;
+        mm[warp * Mg::kCols + col] = m[nt][c];
+        lm[warp * Mg::kCols + col] = l[nt][c];
+      }
+  }
+  named_barrier_sync(1, kDecConsumerWarps * 32);
+
+  const int tid = threadIdx.x;
+  constexpr int kQuads = HD / 4;
+  for (int idx = tid; idx < Mg::kCols * kQuads; idx += kDecConsumerWarps * 32) {
+    const int col = idx / kQuads;
+    const int d4 = (idx % kQuads) * 4;
+    const int rr = row_base + col;
+    if (rr >= rows_total) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecConsumerWarps; ++w) M = fmaxf(M, mm[w * Mg::kCols + col]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kDecConsumerWarps; ++w) {
+        const float f = fast_exp2(mm[w * Mg::kCols + col] - M);
+        L += lm[w * Mg::kCols + col] * f;
+        const float4 ow = *reinterpret_cast<const float4*>(&om[(w * Mg::kCols + col) * Mg::kStride + d4]);
+        acc.x += ow.x * f;
+        acc.y += ow.y * f;
+        acc.z += ow.z * f;
+        acc.w += ow.w * f;
+      }
+    }
+    const int i = rr / p.GQ;
+    const int h = kvh * p.GQ + rr % p.GQ;
+    const size_t R = static_cast<size_t>(b * p.Sq + i) * p.HQ + h;
+    if (p.ows != nullptr) {
+      *reinterpret_cast<float4*>(p.ows + (R * p.NP + z) * HD + d4) = acc;
+      if (d4 == 0) {
+        p.mdws[(R * p.NP + z) * 2] = M;
+        p.mdws[(R * p.NP + z) * 2 + 1] = L;
+      }
+    } else {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      T* op = static_cast<T*>(p.out) + R * HD + d4;
+      uint2 packed;
+      packed.x = Elem<T>::pack(acc.x * inv, acc.y * inv);
+      packed.y = Elem<T>::pack(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(op) = packed;
+      if (d4 == 0 && p.lse != nullptr) p.lse[R] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    }
+  }
+}
+
+// --------------------------------------------------------------- combine
+
+// One warp per query row; lanes own D/32 contiguous columns.  Partial p of
+// row r: o at ows[(r*NP + p)*D], (m, d) at mdws[(r*NP + p)*2].  PACKED_LSE
+// reads per-rank (O, LSE) rows instead: packed[(p*rows + r)*(D+1)] holds the
+// normalised O followed by the natural-log LSE.
+template <typename T, int HD, bool kPackedLse>
+__global__ void __launch_bounds__(128) split_combine_kernel(const float* __restrict__ ows,
+                                                            const float* __restrict__ mdws,
+                                                            T* __restrict__ out, float* __restrict__ out_f32,
+                                                            float* __restrict__ lse, int rows, int NP) {
+  constexpr int kPer = HD / 32;
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float M = -INFINITY, L = 0.f;
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  for (int pz = 0; pz < NP; ++pz) {
+    float mz, dz;
+    const float* src;
+    if constexpr (kPackedLse) {
+      src = ows + (static_cast<size_t>(pz) * rows + r) * (HD + 1);
+      const float lz = src[HD];
+      mz = lz * kLog2e;  // (O, lse) == (o = O, m = lse*log2e, d = 1)
+      dz = 1.f;
+    } else {
+      const size_t pi = static_cast<size_t>(r) * NP + pz;
+      mz = mdws[pi * 2];
+      dz = mdws[pi * 2 + 1];
+      src = ows + pi * HD;
+    }
+    if (!(mz > -INFINITY) || !(dz > 0.f)) continue;
+    const float mn = fmaxf(M, mz);
+    const float f1 = fast_exp2(M - mn);
+    const float f2 = fast_exp2(mz - mn);
+    float vals[kPer];
+    if constexpr (kPer == 4 && !kPackedLse) {
+      const float4 v4 = *reinterpret_cast<const float4*>(src + lane * 4);
+      vals[0] = v4.x; vals[1] = v4.y; vals[2] = v4.z; vals[3] = v4.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) vals[j] = src[lane * kPer + j];
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) acc[j] = acc[j] * f1 + vals[j] * f2;
+    L = L * f1 + dz * f2;
+    M = mn;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (out != nullptr) {
+    T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
+#pragma unroll
+    for (int j = 0; j < kPer; j += 2) *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
+  }
+  if (out_f32 != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) out_f32[static_cast<size_t>(r) * HD + lane * kPer + j] = acc[j] * inv;
+  }
+  if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+}
+
+// ---------------------------------------------------------------- append
+
+struct AppendParams {
+  const uint8_t* k_new;  // [B, Sk, HKV, D]
+  const uint8_t* v_new;
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  const int* bt;         // nullptr: dense cache [B, PS, HKV, D]
+  const int* seqlens;
+  int B, Sk, HKV, row_bytes, PS, BTW, P;
+};
+
+// One thread per 16-byte chunk of an appended row: bit-exact placement of
+// token i of sequence b at logical position seqlens[b] + i.
+__global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
+  const int chunks = p.row_bytes / 16;
+  const long long total = static_cast<long long>(p.B) * p.Sk * p.HKV * chunks;
+  for (long long idx = blockIdx.x * 256LL + threadIdx.x; idx < total; idx += 256LL * gridDim.x) {
+    const int c = static_cast<int>(idx % chunks);
+    long long rest = idx / chunks;
+    const int h = static_cast<int>(rest % p.HKV);
+    rest /= p.HKV;
+    const int i = static_cast<int>(rest % p.Sk);
+    const int b = static_cast<int>(rest / p.Sk);
+    const int pos = p.seqlens[b] + i;
+    int phys = b;
+    int slot = pos;
+    if (p.bt != nullptr) {
+      const int page = pos / p.PS;
+      if (pos < 0 || page >= p.BTW) {
+        raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+        continue;
+      }
+      phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+      slot = pos % p.PS;
+      if (phys < 0 || phys >= p.P) {
+        raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+        continue;
+      }
+    } else if (pos < 0 || pos >= p.PS) {
+      raise_flag(MXFA_FLAG_DENSE_OVERFLOW);
+      continue;
+    }
+    const size_t src = ((static_cast<size_t>(b) * p.Sk + i) * p.HKV + h) * p.row_bytes + c * 16;
+    const size_t dst = ((static_cast<size_t>(phys) * p.PS + slot) * p.HKV + h) * p.row_bytes + c * 16;
+    *reinterpret_cast<uint4*>(p.k_cache + dst) = *reinterpret_cast<const uint4*>(p.k_new + src);
+    *reinterpret_cast<uint4*>(p.v_cache + dst) = *reinterpret_cast<const uint4*>(p.v_new + src);
+  }
+}
+
+__global__ void seqlens_add_kernel(void* seqlens, int is_int64, int B, int delta) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  if (is_int64)
+    static_cast<long long*>(seqlens)[b] += delta;
+  else
+    static_cast<int*>(seqlens)[b] += delta;
+}
+
+}  // namespace mxfa

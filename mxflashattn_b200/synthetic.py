@@ -231,12 +231,19 @@ def device_paged_decode(
     lengths = [int(x) for x in lengths]
     batch = len(lengths)
     width = max((L + spare_pages * page_size + page_size - 1) // page_size for L in lengths)
-    pages = batch * width
+    # allocate exactly the pages the sequences occupy (plus spares), like a paged
+    # serving cache, and scatter them over a random permutation
+    need = [(L + spare_pages * page_size + page_size - 1) // page_size for L in lengths]
+    pages = max(sum(need), 1)
     tdt = torch_dtype(dtype)
     k_cache = torch.randn((pages, page_size, kv_heads, head_dim), generator=gen, device=device, dtype=tdt)
     v_cache = torch.randn((pages, page_size, kv_heads, head_dim), generator=gen, device=device, dtype=tdt)
     perm = torch.randperm(pages, generator=gen, device=device).to(torch.int32)
-    block_table = perm.reshape(batch, width).contiguous()
+    block_table = torch.zeros((batch, width), dtype=torch.int32, device=device)
+    offset = 0
+    for b, n in enumerate(need):
+        block_table[b, :n] = perm[offset:offset + n]
+        offset += n
     q = torch.randn((batch, 1, q_heads, head_dim), generator=gen, device=device, dtype=tdt)
     seqlens = torch.tensor(lengths, dtype=torch.int32, device=device)
     return {"q": q, "k_cache": k_cache, "v_cache": v_cache, "block_table": block_table,

@@ -1,0 +1,239 @@
+"""GPU parity of the split-KV paged decode (and its append) against the oracle.
+
+Every case calls the CUDA library (through the public API, the backend
+module or the reference-compatible C-ABI entry) and compares with the numpy
+oracle restating mxflashattn/reference.py, or with the golden vectors the
+reference itself produced.  Tolerances (north star): max-abs 2e-3 fp16,
+1e-2 bf16, LSE 1e-3; append and block-table indexing bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases as golden_cases
+from helpers import OUT_ATOL, assert_close_lse, assert_close_out, host, oracle_paged, to_device
+from mxflashattn_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+PAGED_GOLDEN = golden_cases.paged_cases()
+
+
+def _no_device_flags():
+    from mxflashattn_b200 import _lib
+
+    assert _lib.read_error_flags() == 0
+
+
+@pytest.mark.parametrize("name", sorted(PAGED_GOLDEN))
+def test_public_api_matches_reference_goldens(name, golden, cuda_device):
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache, get_last_dispatch_info
+
+    case = PAGED_GOLDEN[name]
+    t = to_device(case, cuda_device)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], k=t["k"], v=t["v"],
+                                  cache_seqlens=t["cache_seqlens"], block_table=t["block_table"],
+                                  softmax_scale=case.softmax_scale, causal=case.causal)
+    torch.cuda.synchronize()
+    assert get_last_dispatch_info().backend == "cuda_sm100"
+    assert_close_out(host(out), golden[f"{name}.out_f32"], case.dtype, name)
+    # the reference's own dtype output differs from ours by at most the tolerance too
+    assert_close_out(host(out), golden[f"{name}.out"], case.dtype, name + " (dtype)")
+    if case.k_new is not None:
+        assert golden_cases.digest(host(t["k_cache"])) == golden[f"{name}.k_cache_after_digest"].item()
+        assert golden_cases.digest(host(t["v_cache"])) == golden[f"{name}.v_cache_after_digest"].item()
+        np.testing.assert_array_equal(t["cache_seqlens"].cpu().numpy(), golden[f"{name}.seqlens_after"])
+    _no_device_flags()
+
+
+@pytest.mark.parametrize("name", ["config1", "cov_gq8_d128_bf16", "cov_gq2_d64_fp16", "q3_paged_causal",
+                                  "append_dense_q2_causal"])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_lse_matches_harness_goldens(name, splits, golden, cuda_device):
+    from mxflashattn_b200 import backend
+
+    case = PAGED_GOLDEN[name]
+    t = to_device(case, cuda_device)
+    app = 0
+    if t["k"] is not None:
+        backend.kv_append(t["k_cache"], t["v_cache"], t["k"], t["v"], t["cache_seqlens"], t["block_table"])
+        app = t["k"].shape[1]
+    max_len = int(case.total_lengths.max())
+    chunk = max(16, -(-max_len // splits)) if splits > 1 else 0
+    out, lse = backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                         case.softmax_scale, case.causal, append_len=app, return_lse=True,
+                                         num_splits=splits if splits else 0, chunk_len=chunk)
+    assert_close_out(host(out), golden[f"{name}.out_f32"], case.dtype, name)
+    assert_close_lse(host(lse), golden[f"{name}.lse"], name)
+
+
+COVERAGE = [(gq, d, dt) for gq in (2, 4, 8) for d in (64, 128) for dt in ("fp16", "bf16")]
+
+
+@pytest.mark.parametrize("gq,d,dt", COVERAGE)
+@pytest.mark.parametrize("batch,lengths", [(1, [8192]), (8, [1, 17, 1000, 4096, 33, 15, 16, 2049])])
+def test_shape_coverage_matrix_with_outliers(gq, d, dt, batch, lengths, cuda_device):
+    """Coverage matrix: GQ x D x dtype, Hk=4, lengths incl. non-multiples of 16, 1% x50 outliers."""
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    case = syn.paged_case(1000 + gq * 10 + d + (dt == "bf16"), batch=batch, q_heads=4 * gq, kv_heads=4,
+                          head_dim=d, dtype=dt, page_size=16, lengths=lengths, outlier_frac=0.01)
+    t = to_device(case, cuda_device)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], cache_seqlens=t["cache_seqlens"],
+                                  block_table=t["block_table"], softmax_scale=case.softmax_scale)
+    ref = oracle_paged(case)[0]
+    assert_close_out(host(out), ref, dt, f"gq{gq} d{d} {dt}")
+
+
+@pytest.mark.parametrize("page_size", [1, 2, 4, 8, 16, 32, 48])
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_page_sizes_and_append_are_exact(page_size, dt, cuda_device):
+    """Any page size: TMA tiles for multiples of 16, row gathers otherwise; bit-exact append."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    case = syn.paged_case(77 + page_size, batch=3, q_heads=8, kv_heads=2, head_dim=128, dtype=dt,
+                          page_size=page_size, lengths=[0, 45, 130], append=1)
+    t = to_device(case, cuda_device)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], k=t["k"], v=t["v"],
+                                  cache_seqlens=t["cache_seqlens"], block_table=t["block_table"],
+                                  softmax_scale=case.softmax_scale)
+    torch.cuda.synchronize()
+    ref, _, kc, vc, sl = oracle_paged(case)
+    assert_close_out(host(out), ref, dt, f"ps{page_size}")
+    np.testing.assert_array_equal(host(t["k_cache"]), kc)
+    np.testing.assert_array_equal(host(t["v_cache"]), vc)
+    np.testing.assert_array_equal(t["cache_seqlens"].cpu().numpy(), sl)
+    _no_device_flags()
+
+
+@pytest.mark.parametrize("page_size", [2, 16])
+def test_poisoned_padding_never_leaks(page_size, cuda_device):
+    """Unused slots and pages hold NaN; outputs must stay finite and equal the oracle."""
+    from mxflashattn_b200 import backend
+
+    case = syn.paged_case(5, batch=4, q_heads=16, kv_heads=4, head_dim=128, dtype="bf16", page_size=page_size,
+                          lengths=[1, 17, 31, 100], poison=float("nan"), extra_table_cols=2,
+                          num_pages=400 if page_size == 2 else 40)
+    t = to_device(case, cuda_device)
+    ref = oracle_paged(case)[0]
+    for splits, chunk in ((1, 0), (3, 20), (7, 16)):
+        out = backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                        case.softmax_scale, False, num_splits=splits, chunk_len=chunk)
+        assert_close_out(host(out), ref, "bf16", f"poison ps{page_size} splits{splits}")
+
+
+@pytest.mark.parametrize("q_len,gq", [(1, 8), (2, 4), (3, 8), (5, 4), (16, 2)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_multi_query_rows_causal(q_len, gq, causal, cuda_device):
+    """Sq > 1 (speculative / chunked) rows packed with GQA heads; bottom-right causal."""
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    case = syn.paged_case(300 + q_len * 7 + gq, batch=3, q_heads=2 * gq, kv_heads=2, head_dim=64, dtype="fp16",
+                          page_size=16, lengths=[20, 3, 64], q_len=q_len, append=q_len, causal=causal)
+    t = to_device(case, cuda_device)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], k=t["k"], v=t["v"],
+                                  cache_seqlens=t["cache_seqlens"], block_table=t["block_table"],
+                                  softmax_scale=case.softmax_scale, causal=causal)
+    ref = oracle_paged(case)[0]
+    assert_close_out(host(out), ref, "fp16", f"Sq{q_len} gq{gq} causal={causal}")
+
+
+def test_dense_cache_with_int64_lengths(cuda_device):
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    case = syn.paged_case(41, batch=2, q_heads=4, kv_heads=1, head_dim=128, dtype="bf16", page_size=1,
+                          lengths=[5, 60], append=2, q_len=2, causal=True, dense=True, extra_table_cols=4)
+    t = to_device(case, cuda_device)
+    seq64 = t["cache_seqlens"].to(torch.int64)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], k=t["k"], v=t["v"], cache_seqlens=seq64,
+                                  softmax_scale=case.softmax_scale, causal=True)
+    ref, _, kc, vc, sl = oracle_paged(case)
+    assert_close_out(host(out), ref, "bf16", "dense")
+    np.testing.assert_array_equal(host(t["k_cache"]), kc)
+    assert seq64.dtype == torch.int64 and seq64.cpu().tolist() == sl.tolist()
+
+
+@pytest.mark.parametrize("gq", [2, 4, 8])
+@pytest.mark.parametrize("np_", [1, 2, 5, 16])
+def test_reference_compatible_split_entry(gq, np_, cuda_device):
+    """m1.paged_decode_split keeps the reference binding's contract (NP, c_len from the vLLM heuristic)."""
+    import torch
+
+    from mxflashattn_b200 import m1
+
+    lengths = [700, 1, 1280, 333]
+    case = syn.paged_case(900 + gq + np_, batch=4, q_heads=8 * gq, kv_heads=8, head_dim=128, dtype="bf16",
+                          page_size=16, lengths=lengths)
+    t = to_device(case, cuda_device)
+    msl = case.block_table.shape[1] * 16
+    c_len = (msl + np_ - 1) // np_  # reference c_len: not a multiple of 16 in general
+    out = m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["cache_seqlens"],
+                                case.softmax_scale, torch.cuda.current_stream().cuda_stream, np_, c_len)
+    assert_close_out(host(out), oracle_paged(case)[0], "bf16", f"m1 gq{gq} np{np_}")
+
+
+def test_reference_compatible_split_entry_rejects_like_reference(cuda_device):
+    import torch
+
+    from mxflashattn_b200 import m1
+
+    case = syn.paged_case(5, batch=1, q_heads=12, kv_heads=4, head_dim=128, dtype="fp16", page_size=16,
+                          lengths=[20])
+    t = to_device(case, cuda_device)
+    with pytest.raises(RuntimeError, match="unsupported config"):
+        m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["cache_seqlens"], 0.1,
+                              torch.cuda.current_stream().cuda_stream, 2, 16)
+    with pytest.raises(RuntimeError, match="dtype/layout"):
+        m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"].long(), t["cache_seqlens"],
+                              0.1, 0, 2, 16)
+
+
+def test_qwen3_4b_batch128_sampled_against_oracle(cuda_device):
+    """Benchmark config 2 at full size (B=128, Hq=32, Hk=8, D=128, bf16): sampled rows vs oracle."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    lengths = syn.qwen3_4b_lengths(2026)
+    t = syn.device_paged_decode(seed=7, lengths=lengths, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16",
+                                page_size=16, device=cuda_device)
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], cache_seqlens=t["cache_seqlens"],
+                                  block_table=t["block_table"])
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    rng = np.random.default_rng(0)
+    bt = t["block_table"].cpu().numpy()
+    import oracle
+
+    for b in rng.choice(len(lengths), size=6, replace=False):
+        L = int(lengths[b])
+        kc = oracle.gather_paged_kv(host(t["k_cache"][torch.from_numpy(bt[b]).to(cuda_device).long()]).reshape(
+            -1, 16, 8, 128), np.arange(bt.shape[1]), L)
+        vc = oracle.gather_paged_kv(host(t["v_cache"][torch.from_numpy(bt[b]).to(cuda_device).long()]).reshape(
+            -1, 16, 8, 128), np.arange(bt.shape[1]), L)
+        ref = oracle.attention_single(host(t["q"][b]), kc, vc)
+        err = float(np.max(np.abs(host(out[b]) - ref)))
+        assert err <= OUT_ATOL["bf16"], f"sequence {b} (len {L}): {err:.3e}"
+    _no_device_flags()
+
+
+def test_long_context_16k_split_vs_oracle(cuda_device):
+    """Config 5 decode shape (ctx 16384, Hq=32, Hk=8, D=128, bf16) at batch 1."""
+    from mxflashattn_b200 import backend
+
+    case = syn.paged_case(16384, batch=1, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", page_size=16,
+                          lengths=[16384])
+    t = to_device(case, cuda_device)
+    out, lse = backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                         case.softmax_scale, False, return_lse=True)
+    ref, ref_lse = oracle_paged(case)[:2]
+    assert_close_out(host(out), ref, "bf16", "16k")
+    assert_close_lse(host(lse), ref_lse, "16k")

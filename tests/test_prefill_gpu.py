@@ -1,0 +1,126 @@
+"""GPU parity of the dense / varlen attention forward against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases as golden_cases
+import oracle
+from helpers import assert_close_lse, assert_close_out, host
+from mxflashattn_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+VARLEN_GOLDEN = golden_cases.varlen_cases()
+
+
+def _dev(case, device):
+    import torch
+
+    tdt = syn.torch_dtype(case.dtype)
+    return (torch.from_numpy(case.q).to(device, tdt), torch.from_numpy(case.k).to(device, tdt),
+            torch.from_numpy(case.v).to(device, tdt), torch.from_numpy(case.cu_q).to(device),
+            torch.from_numpy(case.cu_k).to(device))
+
+
+@pytest.mark.parametrize("name", sorted(VARLEN_GOLDEN))
+def test_varlen_matches_reference_goldens(name, golden, cuda_device):
+    from mxflashattn_b200 import flash_attn_varlen_func, get_last_dispatch_info
+
+    case = VARLEN_GOLDEN[name]
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out = flash_attn_varlen_func(q, k, v, cu_q, cu_k, int(np.diff(case.cu_q).max()), int(np.diff(case.cu_k).max()),
+                                 softmax_scale=case.softmax_scale, causal=case.causal)
+    assert get_last_dispatch_info().backend == "cuda_sm100"
+    assert_close_out(host(out), golden[f"{name}.out_f32"], case.dtype, name)
+
+
+@pytest.mark.parametrize("name", ["varlen_causal_bf16", "varlen_causal_d128_gq4"])
+def test_varlen_lse(name, golden, cuda_device):
+    from mxflashattn_b200 import backend
+
+    case = VARLEN_GOLDEN[name]
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    _, lse = backend.flash_attn_varlen_func(q, k, v, cu_q, cu_k, int(np.diff(case.cu_q).max()),
+                                            int(np.diff(case.cu_k).max()), case.causal, case.softmax_scale,
+                                            return_lse=True)
+    assert_close_lse(host(lse), golden[f"{name}.lse"], name)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_dense_batched_forward(dt, d, causal, cuda_device):
+    import torch
+
+    from mxflashattn_b200 import flash_attn_func
+
+    rng = np.random.default_rng(d + causal)
+    q = syn.round_dtype(rng.standard_normal((2, 77, 8, d), dtype=np.float32), dt)
+    k = syn.round_dtype(rng.standard_normal((2, 130, 2, d), dtype=np.float32), dt)
+    v = syn.round_dtype(rng.standard_normal((2, 130, 2, d), dtype=np.float32), dt)
+    tdt = syn.torch_dtype(dt)
+    out = flash_attn_func(torch.from_numpy(q).to(cuda_device, tdt), torch.from_numpy(k).to(cuda_device, tdt),
+                          torch.from_numpy(v).to(cuda_device, tdt), causal=causal)
+    ref = oracle.attention_batched(q, k, v, causal=causal)
+    assert_close_out(host(out), ref, dt, f"dense d{d} causal={causal}")
+
+
+def test_causal_query_longer_than_key_gives_zero_rows(cuda_device):
+    """reference test_api.py:52-62 on the device: rows with no visible key are exactly 0."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_func
+
+    torch.manual_seed(0)
+    q = torch.randn(1, 3, 2, 64, device=cuda_device, dtype=torch.float16)
+    k = torch.randn(1, 1, 1, 64, device=cuda_device, dtype=torch.float16)
+    v = torch.randn_like(k)
+    out = flash_attn_func(q, k, v, causal=True)
+    assert torch.isfinite(out).all()
+    assert torch.equal(out[:, :2], torch.zeros_like(out[:, :2]))
+    torch.testing.assert_close(out[:, 2:], v.expand(-1, -1, 2, -1), rtol=0, atol=1e-3)
+
+
+def test_zero_scale_is_uniform_average(cuda_device):
+    import torch
+
+    from mxflashattn_b200 import flash_attn_func
+
+    torch.manual_seed(1)
+    q = torch.randn(1, 4, 4, 64, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(1, 6, 2, 64, device=cuda_device, dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    out = flash_attn_func(q, k, v, softmax_scale=0.0)
+    expect = v.float().mean(dim=1, keepdim=True).repeat_interleave(2, dim=2).expand(-1, 4, -1, -1)
+    torch.testing.assert_close(out.float(), expect, rtol=0, atol=1e-2)
+
+
+def test_prefill_config_varlen_sampled_rows(cuda_device):
+    """Config 5 prefill ({15000, 1024, 512, 37}, Hq=32, Hk=8, D=128, causal): rows sampled vs oracle."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_varlen_func
+
+    lens = [15000, 1024, 512, 37]
+    case = syn.varlen_case(55, q_lens=lens, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", causal=True)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out = flash_attn_varlen_func(q, k, v, cu_q, cu_k, max(lens), max(lens), causal=True)
+    torch.cuda.synchronize()
+    out_h = host(out)
+    assert np.isfinite(out_h).all()
+    rng = np.random.default_rng(3)
+    for s, L in enumerate(lens):
+        start = int(case.cu_q[s])
+        rows = np.unique(np.concatenate([[0, L - 1], rng.integers(0, L, size=6)]))
+        for h in (0, 13, 31):
+            kh = h // 4
+            keys = case.k[start:start + L, kh]
+            vals = case.v[start:start + L, kh]
+            for r in rows:
+                sc = (keys[: r + 1] @ case.q[start + r, h]) * case.softmax_scale
+                p = np.exp(sc - sc.max())
+                ref = (p / p.sum()) @ vals[: r + 1]
+                err = float(np.max(np.abs(out_h[start + r, h] - ref)))
+                assert err <= 1e-2, f"seq {s} row {r} head {h}: {err:.3e}"
