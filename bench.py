@@ -270,15 +270,36 @@ def run_ours(args):
         sl_host = layers[0]["cache_seqlens"].cpu().pin_memory()
         q_dev = [torch.empty_like(t["q"]) for t in layers]
         sl_dev = torch.empty_like(layers[0]["cache_seqlens"])
+        h2d = torch.cuda.Stream(device)
+        d2h = torch.cuda.Stream(device)
+        ev_in = [torch.cuda.Event() for _ in layers]
+        ev_done = [torch.cuda.Event() for _ in layers]
+        ev_sl = torch.cuda.Event()
 
         def e2e_step_tables():
-            # per step: upload the lengths once and each layer's q, read each layer's output back
-            sl_dev.copy_(sl_host, non_blocking=True)
+            # Copies run on their own streams so layer i+1's upload and layer i's
+            # read-back overlap layer i's kernel; every copy stays inside the
+            # timed region.  q buffers are reused only after the previous
+            # step's kernel that read them has finished.
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(ev_done[-1])  # every layer of the previous step has read sl_dev
+                sl_dev.copy_(sl_host, non_blocking=True)
+                ev_sl.record(h2d)
+                for i in range(len(layers)):
+                    h2d.wait_event(ev_done[i])
+                    q_dev[i].copy_(q_host[i], non_blocking=True)
+                    ev_in[i].record(h2d)
+            stream.wait_event(ev_sl)
             for i, t in enumerate(layers):
-                q_dev[i].copy_(q_host[i], non_blocking=True)
+                stream.wait_event(ev_in[i])
                 o = flash_attn_with_kvcache(q_dev[i], t["k_cache"], t["v_cache"], cache_seqlens=sl_dev,
                                             block_table=t["block_table"], softmax_scale=scale)
-                out_host[i].copy_(o, non_blocking=True)
+                ev_done[i].record(stream)
+                o.record_stream(d2h)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_done[i])
+                    out_host[i].copy_(o, non_blocking=True)
+            stream.wait_stream(d2h)
 
         for _ in range(3):
             e2e_step_tables()

@@ -126,11 +126,9 @@ int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
   const int rows_kv = p.Sq * p.GQ;
   const int nt = rows_kv <= 8 ? 1 : 2;
   const int row_groups = (rows_kv + 8 * nt - 1) / (8 * nt);
-  if (static_cast<long long>(p.HKV) * row_groups > 65535)
-    return fail(MXFA_ERR_UNSUPPORTED, "too many KV heads x query-row groups (%d x %d)", p.HKV, row_groups);
   const int nz = p.ows != nullptr ? p.NP : 1;
-  if (nz > 65535) return fail(MXFA_ERR_UNSUPPORTED, "too many splits (%d)", nz);
-  dim3 grid(p.B, p.HKV * row_groups, nz);
+  if (nz > 65535 || p.B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "too many splits or sequences");
+  dim3 grid(p.HKV * row_groups, p.B, nz);
   CUtensorMap tk, tv;
   std::memset(&tk, 0, sizeof(tk));
   std::memset(&tv, 0, sizeof(tv));
@@ -286,6 +284,9 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
   const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
+  if (static_cast<long long>(num_splits) * chunk_len < max_len)
+    return fail(MXFA_ERR_INVALID, "%d splits of %d positions do not cover the cache capacity %d", num_splits,
+                chunk_len, max_len);
   p.NP = num_splits;
   p.c_len = chunk_len;
   p.ows = static_cast<float*>(workspace);

@@ -182,6 +182,9 @@ struct Elem<__nv_bfloat16> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   static __device__ __forceinline__ __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ float2 unpack(uint32_t v) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+  }
   // D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate.
   static __device__ __forceinline__ void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -200,6 +203,7 @@ struct Elem<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   static __device__ __forceinline__ __half from_float(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ float2 unpack(uint32_t v) { return __half22float2(*reinterpret_cast<__half2*>(&v)); }
   static __device__ __forceinline__ void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(

@@ -46,6 +46,7 @@ struct DecodeParams {
 };
 
 constexpr int kDecConsumerWarps = 4;
+constexpr int kRankMaxBatch = 512;  // batches up to this size are dispatched longest-first
 constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kTileTok = 16;
 
@@ -80,12 +81,34 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + Cfg::kRingBytes);
   uint64_t* empty = full + Cfg::kSlots;
 
-  const int b = blockIdx.x;
-  const int kvh = blockIdx.y % p.HKV;
-  const int rg = blockIdx.y / p.HKV;
+  // Grid: x = (KV head, row group), y = length rank, z = split.  The hardware
+  // dispatches blocks in linear order, so mapping rank y to the y-th longest
+  // sequence starts the longest work first (longest-processing-time order),
+  // which keeps the tail of ragged batches short.
+  const int kvh = blockIdx.x % p.HKV;
+  const int rg = blockIdx.x / p.HKV;
   const int z = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  int b = blockIdx.y;
+  if (p.B > 1 && p.B <= kRankMaxBatch) {
+    __shared__ int s_seq;
+    int* lens = reinterpret_cast<int*>(ring);  // ring is not in use yet
+    for (int i = threadIdx.x; i < p.B; i += blockDim.x) lens[i] = p.seqlens[i];
+    __syncthreads();
+    const int want = blockIdx.y;
+    for (int i = threadIdx.x; i < p.B; i += blockDim.x) {
+      const int li = lens[i];
+      int rank = 0;
+      for (int j = 0; j < p.B; ++j) {
+        const int lj = lens[j];
+        rank += (lj > li) || (lj == li && j < i);
+      }
+      if (rank == want) s_seq = i;
+    }
+    __syncthreads();
+    b = s_seq;
+  }
 
   const int total_len = p.seqlens[b] + p.append_len;
   // split mode (partials written for a combine) whenever a workspace is given;
@@ -325,13 +348,22 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         }
       }
 
-    // P (tok x rows) -> B fragments of the PV product
-    uint32_t pb[NT][2];
+    // P (tok x rows) -> B fragments of the PV product.  P is split into a
+    // rounded high part and the rounded remainder (p = hi + lo to ~16
+    // significant bits) and both are multiplied with V, so the product keeps
+    // fp32-level accuracy even when V carries large outliers; the extra
+    // tensor-core work is free on this memory-bound path.
+    uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      pb[nt][0] = movmatrix_trans(Elem<T>::pack(s[nt][0], s[nt][1]));
-      pb[nt][1] = movmatrix_trans(Elem<T>::pack(s[nt][2], s[nt][3]));
-    }
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float a = s[nt][2 * hh], c = s[nt][2 * hh + 1];
+        const uint32_t hi = Elem<T>::pack(a, c);
+        const float2 hf = Elem<T>::unpack(hi);
+        pb[nt][hh] = movmatrix_trans(hi);
+        pl[nt][hh] = movmatrix_trans(Elem<T>::pack(a - hf.x, c - hf.y));
+      }
     {
       const int q8 = lane >> 3;
       const int r = ((q8 >> 1) << 3) + (lane & 7);
@@ -341,7 +373,10 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         uint32_t a0, a1, a2, a3;
         ldsm_x4_trans(vbase + (dch >> 3) * Cfg::kBlkBytes + swz128(r, dch & 7), a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+        }
       }
     }
     __syncwarp();

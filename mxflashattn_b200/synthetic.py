@@ -238,12 +238,13 @@ def device_paged_decode(
     tdt = torch_dtype(dtype)
     k_cache = torch.randn((pages, page_size, kv_heads, head_dim), generator=gen, device=device, dtype=tdt)
     v_cache = torch.randn((pages, page_size, kv_heads, head_dim), generator=gen, device=device, dtype=tdt)
-    perm = torch.randperm(pages, generator=gen, device=device).to(torch.int32)
-    block_table = torch.zeros((batch, width), dtype=torch.int32, device=device)
+    perm = torch.randperm(pages, generator=gen, device=device).to(torch.int32).cpu().numpy()
+    table = np.zeros((batch, width), dtype=np.int32)
     offset = 0
     for b, n in enumerate(need):
-        block_table[b, :n] = perm[offset:offset + n]
+        table[b, :n] = perm[offset:offset + n]
         offset += n
+    block_table = torch.from_numpy(table).to(device)
     q = torch.randn((batch, 1, q_heads, head_dim), generator=gen, device=device, dtype=tdt)
     seqlens = torch.tensor(lengths, dtype=torch.int32, device=device)
     return {"q": q, "k_cache": k_cache, "v_cache": v_cache, "block_table": block_table,

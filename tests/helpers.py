@@ -8,8 +8,16 @@ import oracle
 from mxflashattn_b200 import synthetic as syn
 
 # Output tolerances against the fp32 oracle: max-abs 2e-3 for
-# fp16, 1e-2 for bf16; LSE within 1e-3.
+# fp16, 1e-2 for bf16; LSE within 1e-3.  An output stored in bf16/fp16 cannot
+# be closer to the fp32 value than half a storage ulp, so where |ref| is large
+# (the x50-outlier cases) the bound is that half ulp instead:
+#     |ours - ref| <= max(atol, half_ulp_rel * |ref|) + extra
+# ``extra`` is used only by the prefill kernel, whose P@V product rounds P to
+# the storage dtype once (as FlashAttention does): its error is at most
+# u_P * sum(p |v|) / sum(p), computed by the oracle as attention over |V|.
 OUT_ATOL = {"fp16": 2e-3, "bf16": 1e-2}
+HALF_ULP_REL = {"fp16": 2.0 ** -11, "bf16": 2.0 ** -8}
+P_ROUND_REL = {"fp16": 2.0 ** -11, "bf16": 2.0 ** -8}
 LSE_ATOL = 1e-3
 
 
@@ -44,10 +52,28 @@ def max_abs(a, b) -> float:
     return float(np.max(np.abs(a - b))) if a.size else 0.0
 
 
-def assert_close_out(actual, expected, dtype, what=""):
-    err = max_abs(actual, expected)
-    assert np.isfinite(np.asarray(actual, np.float64)).all(), f"{what}: non-finite output"
-    assert err <= OUT_ATOL[dtype], f"{what}: max abs err {err:.3e} > {OUT_ATOL[dtype]:.0e} ({dtype})"
+def out_tolerance(expected, dtype, extra=0.0, ulps: float = 1.0):
+    e = np.abs(np.asarray(expected, np.float64))
+    return np.maximum(OUT_ATOL[dtype], ulps * HALF_ULP_REL[dtype] * e * 1.001 + 1e-6 * e) + extra
+
+
+def assert_close_out(actual, expected, dtype, what="", extra=0.0, ulps: float = 1.0):
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert np.isfinite(a).all(), f"{what}: non-finite output"
+    err = np.abs(a - e)
+    tol = out_tolerance(e, dtype, extra, ulps)
+    bad = err > tol
+    if bad.any():
+        i = np.unravel_index(np.argmax(err - tol), err.shape)
+        raise AssertionError(f"{what}: {int(bad.sum())} elements out of tolerance; worst at {i}: "
+                             f"|{a[i]:.6g} - {e[i]:.6g}| = {err[i]:.3e} > {np.broadcast_to(tol, err.shape)[i]:.3e} "
+                             f"({dtype}); max abs err {err.max():.3e}")
+
+
+def p_rounding_bound(dtype, abs_v_attention):
+    """Prefill P-rounding error bound: u_P * (softmax-weighted mean of |V|)."""
+    return P_ROUND_REL[dtype] * np.abs(np.asarray(abs_v_attention, np.float64)) * 1.01 + 1e-6
 
 
 def assert_close_lse(actual, expected, what=""):
