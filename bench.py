@@ -39,7 +39,7 @@ WORKLOAD = "qwen3-4b paged decode attention, b128, 36 layers (config 2)"
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS)
@@ -80,27 +80,35 @@ def cpu_model() -> str:
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons; ``summary`` keeps the
+    samples whose timestamps fall inside the marked timed window."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, interval_ms: int = 50):
         self.device_index = device_index
+        self.interval_ms = interval_ms
         self.proc = None
+        self.window = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                 str(self.interval_ms), "-i", str(self.device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        time.sleep(0.5)  # let nvidia-smi attach before the timed region
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -111,22 +119,30 @@ class ClockSampler:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
+        import datetime
+
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in getattr(self, "lines", []):
+        parsed = []
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                parsed.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        inside = parsed
+        if self.window is not None and parsed:
+            t0, t1 = self.window
+            inside = [x for x in parsed if t0 - 0.06 <= x[0] <= t1 + 0.06]
+            if not inside:  # window shorter than one interval: nearest sample
+                inside = [min(parsed, key=lambda x: abs(x[0] - (t0 + t1) / 2))]
+        reasons = sorted({n for x in inside for n, v in zip(names, x[3]) if v.lower() == "active"})
+        sm = [x[1] for x in inside]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max((x[2] for x in inside), default=None),
+                "reasons": reasons, "samples": len(sm)}
 
 
 # --------------------------------------------------------------- reference
@@ -244,12 +260,15 @@ def run_ours(args):
                     for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clocks:
-        t_start.record(stream)
-        for s in range(args.steps):
-            step(layer_events[s])
-        t_end.record(stream)
-        torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index).start()
+    w0 = time.time()
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(layer_events[s])
+    t_end.record(stream)
+    torch.cuda.synchronize(device)
+    clocks.mark(w0, time.time())
+    clocks.stop()
     barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
     launch_ms = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for evs in layer_events for i in range(args.layers)]

@@ -56,7 +56,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB_PATH
     tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES]]
+    extra = os.environ.get("MXFA_NVCC_EXTRA", "").split()
+    cmd = [nvcc_path(), *NVCC_FLAGS, *extra, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES]]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

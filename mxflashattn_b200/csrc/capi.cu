@@ -105,7 +105,7 @@ int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, 
                        cudaStream_t st) {
   static std::atomic<unsigned long long> done{0};
   auto kern = paged_decode_kernel<T, HD, NT, kTma>;
-  const int smem = DecodeCfg<HD>::kSmemBytes;
+  const int smem = DecodeCfg<HD, NT>::kSmemBytes;
   if (int rc = ensure_smem(kern, smem, done)) return rc;
   kern<<<grid, kDecThreads, smem, st>>>(p, tk, tv);
   return check_launch("paged_decode_kernel");

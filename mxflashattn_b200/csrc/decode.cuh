@@ -50,13 +50,22 @@ constexpr int kRankMaxBatch = 512;  // batches up to this size are dispatched lo
 constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kTileTok = 16;
 
-template <int HD>
+// Per-instantiation occupancy.  Several CTAs per SM overlap one CTA's
+// start-up and final merge with the others' streaming, which measured worth
+// more than a deeper ring: the shared-memory budget (~192 KB of ring per SM)
+// is split over as many CTAs as the register file allows.
+//   HD=128, 8 query rows : 3 CTAs x 8 slots  (64 KB ring each, <=136 regs)
+//   HD=128, 16 query rows: 2 CTAs x 12 slots (96 KB)
+//   HD=64,  8 query rows : 4 CTAs x 12 slots (48 KB, <=102 regs)
+//   HD=64,  16 query rows: 3 CTAs x 16 slots (64 KB)
+template <int HD, int NT>
 struct DecodeCfg {
+  static constexpr int kCtasPerSm = HD == 128 ? (NT == 1 ? 3 : 2) : (NT == 1 ? 4 : 3);
   static constexpr int kDBlk = HD / 64;                  // 128-byte column blocks per row
   static constexpr int kBlkBytes = kTileTok * 128;       // one column block of one tile: 2 KB
   static constexpr int kTileBytes = kTileTok * HD * 2;   // K (or V) bytes of one tile
   static constexpr int kSlotBytes = 2 * kTileBytes;      // K + V
-  static constexpr int kSlots = (HD == 128) ? 12 : 24;   // 96 KB ring either way
+  static constexpr int kSlots = (192 * 1024 / kCtasPerSm) / kSlotBytes / 4 * 4;  // multiple of the consumer count
   static constexpr int kRingBytes = kSlots * kSlotBytes;
   static constexpr int kSmemBytes = kRingBytes + 2 * kSlots * 8 + 1024;
 };
@@ -71,10 +80,10 @@ struct DecodeMerge {
 };
 
 template <typename T, int HD, int NT, bool kTma>
-__global__ void __launch_bounds__(kDecThreads, 2)
+__global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
-  using Cfg = DecodeCfg<HD>;
+  using Cfg = DecodeCfg<HD, NT>;
   static_assert(DecodeMerge<HD, NT>::kBytes <= Cfg::kRingBytes, "merge scratch must fit the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -322,6 +331,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       }
 
     // online softmax per query row (a column of S^T)
+    float alpha[NT][2];
+    bool grew = false;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -331,22 +342,31 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m[nt][c], mx);
-        float alpha = 1.f, p0 = 0.f, p1 = 0.f;
+        float a = 1.f, p0 = 0.f, p1 = 0.f;
         if (m_new != -INFINITY) {
-          alpha = fast_exp2(m[nt][c] - m_new);
+          a = fast_exp2(m[nt][c] - m_new);
           p0 = fast_exp2(s[nt][c] - m_new);
           p1 = fast_exp2(s[nt][c + 2] - m_new);
         }
-        l[nt][c] = l[nt][c] * alpha + p0 + p1;
+        grew |= m_new != m[nt][c];
+        alpha[nt][c] = a;
+        l[nt][c] = l[nt][c] * a + p0 + p1;
         m[nt][c] = m_new;
         s[nt][c] = p0;
         s[nt][c + 2] = p1;
+      }
+    // the running max rarely moves after the first tiles: rescale O only when it did
+    if (__any_sync(0xffffffffu, grew)) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int mi = 0; mi < HD / 16; ++mi) {
-          o[mi][nt][c] *= alpha;
-          o[mi][nt][c + 2] *= alpha;
+          o[mi][nt][0] *= alpha[nt][0];
+          o[mi][nt][1] *= alpha[nt][1];
+          o[mi][nt][2] *= alpha[nt][0];
+          o[mi][nt][3] *= alpha[nt][1];
         }
-      }
+    }
 
     // P (tok x rows) -> B fragments of the PV product.  P is split into a
     // rounded high part and the rounded remainder (p = hi + lo to ~16
