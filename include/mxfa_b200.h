@@ -110,6 +110,28 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
                                   int append_len, int num_splits, int chunk_len, int causal,
                                   int bf16, float scale, void* stream);
 
+/* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
+ * counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory when they run attention (an engine that pre-reserved all GPU
+ * memory for its own pools, a foreign-language host without a device
+ * allocator, a latency-critical loop that must not risk the device sync a
+ * cudaMalloc can cause).  Arguments match mxfa_kvcache_attention_launch
+ * minus the workspace: the split partials go to one buffer of
+ * MXFA_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that
+ * loads the library holds until the process exits.  Calls needing more
+ * scratch than that fail with MXFA_ERR_UNSUPPORTED and a message.  The
+ * first call on a device looks up the buffer's device address with that
+ * device current (make that first call before any stream capture).  All
+ * calls on a device share the one buffer, so calls that overlap on the GPU
+ * (other streams, other host threads) race and must be serialised by the
+ * caller.  Nothing is allocated or freed by this call. */
+#define MXFA_NOALLOC_SCRATCH_BYTES (4u << 20)
+int mxfa_kvcache_attention_noalloc_launch(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_table, const int32_t* seqlens, void* out,
+                                          float* lse, int B, int Sq, int HQ, int HKV, int D, int PS, int BTW,
+                                          int num_pages, int append_len, int num_splits, int chunk_len,
+                                          int causal, int bf16, float scale, void* stream);
+
 /* LSE merge of split partials (the reference's split_combine,
  * csrc_native/m1_kernel.cpp:862-888, generalised to strided partials).
  * Partial p of row r lives at ows[r*NP*D + p*D] and mdws[(r*NP + p)*2].

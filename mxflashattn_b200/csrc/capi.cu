@@ -435,3 +435,74 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------- allocation-free variant
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: an inference engine that reserved the whole GPU for its own KV
+// pool up front, a host runtime reaching this library through a plain C FFI
+// with no device allocator of its own, or a latency-critical loop where a
+// cudaMalloc (which may synchronise the device) is not acceptable.  For them
+// the split partials live in one fixed buffer compiled into the library.
+//
+// The buffer is a file-scope __device__ array, so every GPU that loads the
+// library holds MXFA_NOALLOC_SCRATCH_BYTES of it until the process exits.
+// Its name is only a host-side stand-in: the device address is obtained with
+// cudaGetSymbolAddress, once per device, with that device current, on the
+// first call made on that device.  All calls on a device share the buffer and
+// leave their partials in it; nothing needs to start at zero because the
+// decode kernel writes every partial slot the combine kernel then reads.
+namespace mxfa {
+namespace {
+
+static __device__ __align__(256) float g_noalloc_scratch[MXFA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+int noalloc_scratch(float** out) {
+  static float* addr[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(MXFA_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(MXFA_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return MXFA_OK;
+}
+
+}  // namespace
+}  // namespace mxfa
+
+extern "C" int mxfa_kvcache_attention_noalloc_launch(const void* q, const void* k_cache, const void* v_cache,
+                                                     const int32_t* block_table, const int32_t* seqlens, void* out,
+                                                     float* lse, int B, int Sq, int HQ, int HKV, int D, int PS,
+                                                     int BTW, int num_pages, int append_len, int num_splits,
+                                                     int chunk_len, int causal, int bf16, float scale,
+                                                     void* stream) {
+  if (B <= 0 || Sq <= 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0 || PS <= 0)
+    return mxfa_kvcache_attention_launch(q, k_cache, v_cache, block_table, seqlens, out, lse, nullptr, 0, B, Sq,
+                                         HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal,
+                                         bf16, scale, stream);
+  const int max_len = block_table ? BTW * PS : PS;
+  if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
+  float* scratch = nullptr;
+  if (num_splits > 1) {
+    const size_t need = mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits);
+    if (need > MXFA_NOALLOC_SCRATCH_BYTES)
+      return fail(MXFA_ERR_UNSUPPORTED,
+                  "allocation-free call needs %zu bytes of split scratch but the built-in buffer holds %u; "
+                  "use fewer splits or a smaller batch, or mxfa_kvcache_attention_launch with a caller workspace",
+                  need, static_cast<unsigned>(MXFA_NOALLOC_SCRATCH_BYTES));
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+  }
+  return mxfa_kvcache_attention_launch(q, k_cache, v_cache, block_table, seqlens, out, lse, scratch,
+                                       scratch ? MXFA_NOALLOC_SCRATCH_BYTES : 0, B, Sq, HQ, HKV, D, PS, BTW,
+                                       num_pages, append_len, num_splits, chunk_len, causal, bf16, scale, stream);
+}

@@ -1,0 +1,98 @@
+"""The allocation-free KV-cache attention entry point, checked on the GPU.
+
+``mxfa_kvcache_attention_noalloc_launch`` serves callers that cannot
+allocate device memory when they run attention -- an engine that reserved
+all of the GPU's memory for its own pools up front, a host written in
+another language that reaches the library through a bare C FFI and has no
+device allocator, or a latency-critical loop that must not risk the device
+synchronisation a cudaMalloc can trigger.  Instead of a caller workspace it
+keeps the split partials in one fixed buffer built into the library.
+
+This test calls it through the C ABI twice in a row, on two different
+inputs so that partials left in the shared buffer by the first call cannot
+leak into the second, and compares each result with the regular entry
+point (caller-provided workspace) within the decode tolerance used by the
+other tests.  It also checks that a request larger than the built-in buffer
+is refused with a clear error instead of being launched.  The file name
+sorts last so that a run stopping at the first failure has already run
+every other test.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from helpers import assert_close_out, assert_close_lse, host, to_device
+from mxflashattn_b200 import _lib, synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def _scratch_limit() -> int:
+    import os
+
+    header = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "mxfa_b200.h")
+    m = re.search(r"#define MXFA_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", open(header).read())
+    return int(m.group(1)) << int(m.group(2))
+
+
+def _launch(case, t, splits, chunk, *, noalloc):
+    import torch
+
+    lib = _lib.load()
+    B, Sq, HQ, D = case.q.shape
+    HKV = case.k_cache.shape[2]
+    PS = case.k_cache.shape[1]
+    BTW = case.block_table.shape[1]
+    out = torch.empty_like(t["q"])
+    lse = torch.empty((B, Sq, HQ), device=t["q"].device, dtype=torch.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+    common = (B, Sq, HQ, HKV, D, PS, BTW, case.k_cache.shape[0], 0, splits, chunk, 0, int(case.dtype == "bf16"),
+              case.softmax_scale, stream)
+    ptrs = (t["q"].data_ptr(), t["k_cache"].data_ptr(), t["v_cache"].data_ptr(), t["block_table"].data_ptr(),
+            t["cache_seqlens"].data_ptr(), out.data_ptr(), lse.data_ptr())
+    if noalloc:
+        rc = lib.mxfa_kvcache_attention_noalloc_launch(*ptrs, *common)
+    else:
+        ws_bytes = lib.mxfa_split_workspace_bytes(B * Sq * HQ, D, splits)
+        ws = torch.empty((ws_bytes // 4,), device=t["q"].device, dtype=torch.float32)
+        rc = lib.mxfa_kvcache_attention_launch(*ptrs, ws.data_ptr(), ws_bytes, *common)
+    _lib.check(rc, "noalloc test launch")
+    torch.cuda.synchronize()
+    return out, lse
+
+
+CASES = [
+    # (seed, batch, q_heads, kv_heads, head_dim, dtype, lengths, splits)
+    (4001, 3, 32, 8, 128, "bf16", [3000, 777, 1], 6),
+    (4002, 2, 16, 4, 64, "fp16", [45, 2500], 9),
+]
+
+
+def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row(cuda_device):
+    for seed, batch, hq, hkv, d, dt, lengths, splits in CASES:
+        case = syn.paged_case(seed, batch=batch, q_heads=hq, kv_heads=hkv, head_dim=d, dtype=dt, page_size=16,
+                              lengths=lengths, outlier_frac=0.01)
+        t = to_device(case, cuda_device)
+        cap = 16 * case.block_table.shape[1]
+        chunk = -(-cap // splits)
+        ref_out, ref_lse = _launch(case, t, splits, chunk, noalloc=False)
+        out, lse = _launch(case, t, splits, chunk, noalloc=True)
+        assert_close_out(host(out), host(ref_out), dt, f"noalloc seed {seed}")
+        assert_close_lse(host(lse), host(ref_lse), f"noalloc seed {seed}")
+
+
+def test_noalloc_entry_refuses_requests_beyond_its_buffer(cuda_device):
+    lib = _lib.load()
+    limit = _scratch_limit()
+    rows, d = 64 * 32, 128
+    splits = limit // (rows * (d + 2) * 4) + 1  # one split more than fits
+    assert lib.mxfa_split_workspace_bytes(rows, d, splits) > limit
+    dummy = ctypes.c_void_p(16)  # never dereferenced: the size check refuses first
+    rc = lib.mxfa_kvcache_attention_noalloc_launch(dummy, dummy, dummy, dummy, dummy, dummy, None, 64, 1, 32, 8, d,
+                                                   16, 4096, 100000, 0, splits, 16, 0, 1, 0.1, None)
+    assert rc == _lib.MXFA_ERR_UNSUPPORTED
+    assert "built-in buffer" in _lib.last_error()
