@@ -23,15 +23,23 @@ from . import _lib
 SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
 
 
+_AVAILABLE: dict[int, bool] = {}
+
+
 def is_available() -> bool:
-    """True when a CUDA device of compute capability 10.0 and the library are usable."""
+    """True when the current CUDA device is sm_100 and the library is usable (cached per device)."""
     if not torch.cuda.is_available():
         return False
+    dev = torch.cuda.current_device()
+    cached = _AVAILABLE.get(dev)
+    if cached is not None:
+        return cached
     try:
-        lib = _lib.load()
+        ok = bool(_lib.load().mxfa_is_available())
     except _lib.NativeLibraryError:
-        return False
-    return bool(lib.mxfa_is_available())
+        ok = False
+    _AVAILABLE[dev] = ok
+    return ok
 
 
 def _bf16(t: torch.Tensor) -> int:
@@ -89,14 +97,22 @@ def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False)
 
 # ------------------------------------------------------------------ decode
 
+_PLANS: dict[tuple, tuple[int, int]] = {}
+
+
 def kvcache_plan(batch: int, q_len: int, q_heads: int, kv_heads: int, head_dim: int, max_len: int):
-    """(num_splits, chunk_len) the library picks for this shape on the current device."""
+    """(num_splits, chunk_len) the library picks for this shape on the current device (cached)."""
     import ctypes
 
-    np_, cl = ctypes.c_int(0), ctypes.c_int(0)
-    _lib.check(_lib.load().mxfa_kvcache_plan(batch, q_len, q_heads, kv_heads, head_dim, max_len,
-                                              ctypes.byref(np_), ctypes.byref(cl)), "mxfa_kvcache_plan")
-    return int(np_.value), int(cl.value)
+    key = (torch.cuda.current_device() if torch.cuda.is_available() else -1, batch, q_len, q_heads, kv_heads,
+           head_dim, max_len)
+    plan = _PLANS.get(key)
+    if plan is None:
+        np_, cl = ctypes.c_int(0), ctypes.c_int(0)
+        _lib.check(_lib.load().mxfa_kvcache_plan(batch, q_len, q_heads, kv_heads, head_dim, max_len,
+                                                  ctypes.byref(np_), ctypes.byref(cl)), "mxfa_kvcache_plan")
+        plan = _PLANS[key] = (int(np_.value), int(cl.value))
+    return plan
 
 
 def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
