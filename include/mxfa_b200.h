@@ -140,6 +140,21 @@ int mxfa_kvcache_attention_noalloc_launch(const void* q, const void* k_cache, co
 int mxfa_split_combine_launch(const float* ows, const float* mdws, void* out, float* out_f32,
                               float* lse, int rows, int D, int NP, int bf16, void* stream);
 
+/* Context-split decode, local half (no reference counterpart: the reference
+ * is single-device).  Single-token attention of q [B, 1, HQ, D] over this
+ * rank's positions of every sequence (its own pages, lengths and table),
+ * written as packed f32 [B*HQ, D + 1]: the normalised O of each row followed
+ * by its natural-log LSE (-inf, with O = 0, for a row with no local keys).
+ * That packed buffer is what the ranks all-gather before
+ * mxfa_lse_merge_launch.  Needs a split workspace of
+ * mxfa_split_workspace_bytes(B*HQ, D, num_splits) bytes (num_splits 0 =
+ * library plan, which then needs the plan's size). */
+int mxfa_kvcache_attention_packed_launch(const void* q, const void* k_cache, const void* v_cache,
+                                         const int32_t* block_table, const int32_t* seqlens, float* packed,
+                                         void* workspace, size_t workspace_bytes, int B, int HQ, int HKV,
+                                         int D, int PS, int BTW, int num_pages, int num_splits, int chunk_len,
+                                         int bf16, float scale, void* stream);
+
 /* Merge of per-rank (O, LSE) results for context-split decode across GPUs
  * (no reference counterpart: the reference is single-device).  `packed` is
  * f32 [N, rows, D + 1]: normalised O then the natural-log LSE of each row on

@@ -44,6 +44,8 @@ SIGNATURES = {
              _f, _vp]),
     "mxfa_kvcache_attention_noalloc_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+    "mxfa_kvcache_attention_packed_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "mxfa_split_combine_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mxfa_lse_merge_launch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mxfa_kv_append_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),

@@ -208,6 +208,36 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_tabl
     return out
 
 
+def kvcache_attention_packed(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, *,
+                             num_splits: int = 0, chunk_len: int = 0, out=None):
+    """Local half of a context-split decode: packed f32 [B*HQ, D+1] = (normalised O, LSE) per row."""
+    B, Sq, HQ, D = q.shape
+    if Sq != 1:
+        raise ValueError("packed local attention takes one query token per sequence")
+    q = _contig(q)
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("the CUDA backend requires contiguous k_cache / v_cache")
+    seq = _i32(cache_seqlens)
+    bt = None if block_table is None else _i32(block_table)
+    PS, HKV = k_cache.shape[1], k_cache.shape[2]
+    btw = 0 if bt is None else bt.shape[1]
+    max_len = btw * PS if bt is not None else PS
+    if num_splits <= 0 or chunk_len <= 0:
+        num_splits, chunk_len = kvcache_plan(B, 1, HQ, HKV, D, max_len)
+    lib = _lib.load()
+    ws_bytes = int(lib.mxfa_split_workspace_bytes(B * HQ, D, num_splits))
+    ws = torch.empty((max(ws_bytes, 16) // 4,), device=q.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty((B * HQ, D + 1), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        rc = lib.mxfa_kvcache_attention_packed_launch(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), out.data_ptr(),
+            ws.data_ptr(), ws_bytes, B, HQ, HKV, D, PS, btw, k_cache.shape[0], num_splits, chunk_len, _bf16(q),
+            float(softmax_scale), _stream(q))
+    _lib.check(rc, "mxfa_kvcache_attention_packed_launch")
+    return out
+
+
 # ------------------------------------------------------ combine / merge
 
 def split_combine(ows, mdws, rows: int, head_dim: int, num_splits: int, dtype, *, lse: bool = False,

@@ -186,6 +186,14 @@ void plan_splits(int B, int HKV, int row_groups, int max_len, int* np_out, int* 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+template <int HD>
+int launch_packed_combine(const float* ows, const float* mdws, float* packed, int rows, int NP, cudaStream_t st) {
+  if (rows == 0) return MXFA_OK;
+  split_combine_kernel<__nv_bfloat16, HD, false, true>
+      <<<(rows + 3) / 4, 128, 0, st>>>(ows, mdws, nullptr, packed, nullptr, rows, NP);
+  return check_launch("split_combine_kernel(packed)");
+}
+
 }  // namespace
 }  // namespace mxfa
 
@@ -334,6 +342,54 @@ int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
   return run_combine<false>(p.ows, p.mdws, out, nullptr, nullptr, B * HQ, D, NP, bf16 != 0, st);
+}
+
+int mxfa_kvcache_attention_packed_launch(const void* q, const void* k_cache, const void* v_cache,
+                                         const int32_t* block_table, const int32_t* seqlens, float* packed,
+                                         void* workspace, size_t workspace_bytes, int B, int HQ, int HKV, int D,
+                                         int PS, int BTW, int num_pages, int num_splits, int chunk_len, int bf16,
+                                         float scale, void* stream) {
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (B < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
+    return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d HQ=%d HKV=%d)", B, HQ, HKV);
+  if (B == 0) return MXFA_OK;
+  if (PS <= 0 || num_pages <= 0) return fail(MXFA_ERR_INVALID, "bad cache geometry");
+  if (block_table != nullptr && BTW <= 0) return fail(MXFA_ERR_INVALID, "block table width must be positive");
+  if (!q || !k_cache || !v_cache || !seqlens || !packed) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
+  const int max_len = block_table ? BTW * PS : PS;
+  if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, 1, HQ, HKV, D, max_len, &num_splits, &chunk_len);
+  if (static_cast<long long>(num_splits) * chunk_len < max_len)
+    return fail(MXFA_ERR_INVALID, "%d splits of %d positions do not cover the cache capacity %d", num_splits,
+                chunk_len, max_len);
+  const int rows = B * HQ;
+  const size_t need = mxfa_split_workspace_bytes(rows, D, num_splits);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
+  DecodeParams p{};
+  p.q = q;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.bt = block_table;
+  p.seqlens = seqlens;
+  p.B = B;
+  p.Sq = 1;
+  p.HQ = HQ;
+  p.HKV = HKV;
+  p.PS = PS;
+  p.BTW = block_table ? BTW : 1;
+  p.P = num_pages;
+  p.GQ = HQ / HKV;
+  p.NP = num_splits;
+  p.c_len = chunk_len;
+  p.scale_log2 = scale * kLog2e;
+  p.ows = static_cast<float*>(workspace);
+  p.mdws = p.ows + static_cast<size_t>(rows) * num_splits * D;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
+  return D == 128 ? launch_packed_combine<128>(p.ows, p.mdws, packed, rows, num_splits, st)
+                  : launch_packed_combine<64>(p.ows, p.mdws, packed, rows, num_splits, st);
 }
 
 int mxfa_split_combine_launch(const float* ows, const float* mdws, void* out, float* out_f32, float* lse, int rows,

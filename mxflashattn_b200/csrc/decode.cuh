@@ -493,7 +493,9 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
 // row r: o at ows[(r*NP + p)*D], (m, d) at mdws[(r*NP + p)*2].  PACKED_LSE
 // reads per-rank (O, LSE) rows instead: packed[(p*rows + r)*(D+1)] holds the
 // normalised O followed by the natural-log LSE.
-template <typename T, int HD, bool kPackedLse>
+// With kPackedOut the f32 result is written packed per row, O then LSE
+// ([rows, D+1]): the record one rank contributes to a context-split merge.
+template <typename T, int HD, bool kPackedLse, bool kPackedOut = false>
 __global__ void __launch_bounds__(128) split_combine_kernel(const float* __restrict__ ows,
                                                             const float* __restrict__ mdws,
                                                             T* __restrict__ out, float* __restrict__ out_f32,
@@ -543,11 +545,18 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const float* __restr
 #pragma unroll
     for (int j = 0; j < kPer; j += 2) *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
   }
-  if (out_f32 != nullptr) {
+  if constexpr (kPackedOut) {
+    float* row = out_f32 + static_cast<size_t>(r) * (HD + 1);
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) out_f32[static_cast<size_t>(r) * HD + lane * kPer + j] = acc[j] * inv;
+    for (int j = 0; j < kPer; ++j) row[lane * kPer + j] = acc[j] * inv;
+    if (lane == 0) row[HD] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  } else {
+    if (out_f32 != nullptr) {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) out_f32[static_cast<size_t>(r) * HD + lane * kPer + j] = acc[j] * inv;
+    }
+    if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
   }
-  if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
 }
 
 // ---------------------------------------------------------------- append

@@ -1,0 +1,92 @@
+"""Context-split decode kernels on the GPU.
+
+Ranks are emulated on one device: each rank's packed (O, LSE) record comes
+from ``mxfa_kvcache_attention_packed_launch`` over its own page range, the
+records are stacked as an all-gather would leave them, and
+``mxfa_lse_merge_launch`` merges them.  The result must match attention over
+the whole context (oracle).  When two GPUs are visible, the same path also
+runs with real NCCL ranks.
+"""
+
+from __future__ import annotations
+
+import datetime
+import socket
+
+import numpy as np
+import pytest
+
+from helpers import assert_close_lse, assert_close_out, host, oracle_paged
+from mxflashattn_b200 import context_split as cs
+from mxflashattn_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def _case():
+    return syn.paged_case(123, batch=4, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", page_size=16,
+                          lengths=[16384, 3000, 17, 1], outlier_frac=0.01)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_emulated_ranks_merge_to_full_attention(world, cuda_device):
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    case = _case()
+    tdt = syn.torch_dtype(case.dtype)
+    q = torch.from_numpy(case.q).to(cuda_device, tdt)
+    kc = torch.from_numpy(case.k_cache).to(cuda_device, tdt)
+    vc = torch.from_numpy(case.v_cache).to(cuda_device, tdt)
+    records = []
+    for rank in range(world):
+        ll, table = cs.local_view(case.cache_seqlens, case.block_table, world, rank, 16)
+        records.append(backend.kvcache_attention_packed(q, kc, vc, torch.from_numpy(ll).to(cuda_device),
+                                                        torch.from_numpy(table).to(cuda_device),
+                                                        case.softmax_scale))
+    gathered = torch.stack(records)
+    out, lse = backend.lse_merge(gathered, 4 * 32, 128, tdt, lse=True)
+    ref, ref_lse = oracle_paged(case)[:2]
+    assert_close_out(host(out).reshape(ref.shape), ref, "bf16", f"context split world={world}")
+    assert_close_lse(host(lse).reshape(4, 1, 32), ref_lse, f"context split world={world}")
+
+
+def _nccl_worker(rank, world, port, result):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        case = _case()
+        tdt = syn.torch_dtype(case.dtype)
+        dev = torch.device("cuda", rank)
+        ll, table = cs.local_view(case.cache_seqlens, case.block_table, world, rank, 16)
+        out = cs.context_parallel_decode(torch.from_numpy(case.q).to(dev, tdt),
+                                         torch.from_numpy(case.k_cache).to(dev, tdt),
+                                         torch.from_numpy(case.v_cache).to(dev, tdt),
+                                         torch.from_numpy(ll).to(dev), torch.from_numpy(table).to(dev),
+                                         case.softmax_scale)
+        torch.cuda.synchronize()
+        ref = oracle_paged(case)[0]
+        result[rank] = float(np.max(np.abs(host(out) - ref)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_nccl_context_split(cuda_device):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    manager = mp.Manager()
+    result = manager.dict()
+    mp.spawn(_nccl_worker, args=(2, port, result), nprocs=2, join=True)
+    assert all(result[r] <= 1e-2 for r in range(2)), dict(result)
