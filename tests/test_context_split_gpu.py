@@ -16,7 +16,7 @@ import socket
 import numpy as np
 import pytest
 
-from helpers import assert_close_lse, assert_close_out, host, oracle_paged
+from helpers import assert_close_lse, assert_close_out, host, oracle_paged, out_tolerance
 from mxflashattn_b200 import context_split as cs
 from mxflashattn_b200 import synthetic as syn
 
@@ -71,7 +71,8 @@ def _nccl_worker(rank, world, port, result):
                                          case.softmax_scale)
         torch.cuda.synchronize()
         ref = oracle_paged(case)[0]
-        result[rank] = float(np.max(np.abs(host(out) - ref)))
+        excess = np.abs(host(out) - ref) - out_tolerance(ref, "bf16")
+        result[rank] = float(np.max(excess))  # <= 0 when every element is within tolerance
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -89,4 +90,4 @@ def test_two_gpu_nccl_context_split(cuda_device):
     manager = mp.Manager()
     result = manager.dict()
     mp.spawn(_nccl_worker, args=(2, port, result), nprocs=2, join=True)
-    assert all(result[r] <= 1e-2 for r in range(2)), dict(result)
+    assert all(result[r] <= 0.0 for r in range(2)), dict(result)
