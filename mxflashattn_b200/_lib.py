@@ -51,7 +51,7 @@ SIGNATURES = {
     "mxfa_kv_append_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "mxfa_seqlens_add_launch": (_i, [_vp, _i, _i, _i, _vp]),
     "mxfa_varlen_fwd_launch": (
-        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
 }
 
 _lock = threading.Lock()

@@ -75,8 +75,8 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     with torch.cuda.device(q.device):
         rc = _lib.load().mxfa_varlen_fwd_launch(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_q.data_ptr(), cu_k.data_ptr(), out.data_ptr(),
-            _lib.ptr(lse), batch, int(max_seqlen_q), int(max_seqlen_k), q.shape[1], k.shape[1], q.shape[2],
-            int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
+            _lib.ptr(lse), batch, int(max_seqlen_q), int(max_seqlen_k), q.shape[0], k.shape[0], q.shape[1],
+            k.shape[1], q.shape[2], int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
     _lib.check(rc, "mxfa_varlen_fwd_launch")
     return (out, lse) if return_lse else out
 
@@ -90,7 +90,8 @@ def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False)
     with torch.cuda.device(q.device):
         rc = _lib.load().mxfa_varlen_fwd_launch(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None, out.data_ptr(), _lib.ptr(lse), B, Sq,
-            k.shape[1], HQ, k.shape[2], D, int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
+            k.shape[1], B * Sq, B * k.shape[1], HQ, k.shape[2], D, int(bool(causal)), _bf16(q),
+            float(softmax_scale), _stream(q))
     _lib.check(rc, "mxfa_varlen_fwd_launch")
     return (out, lse) if return_lse else out
 

@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB_NAME = "libmxfa_b200.so"
 LIB_PATH = os.path.join(PKG, LIB_NAME)
 SOURCES = ["capi.cu"]
-HEADERS = ["common.cuh", "decode.cuh", "prefill_mma.cuh"]
+HEADERS = ["common.cuh", "decode.cuh", "prefill_sm100.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

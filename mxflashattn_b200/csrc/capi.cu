@@ -13,8 +13,10 @@
 #include <cstring>
 #include <mutex>
 
+#include <cstdlib>
+
 #include "decode.cuh"
-#include "prefill_mma.cuh"
+#include "prefill_sm100.cuh"
 
 namespace mxfa {
 
@@ -79,6 +81,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
   });
   return fn;
+}
+
+// 3-D map over a [rows][heads][D] tensor with a (64 columns, 1 head,
+// box_rows rows) box and 128-byte swizzle.
+bool encode_rows_map(CUtensorMap* map, const void* base, int D, int heads, long long rows, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  if (rows <= 0 || rows > 0xFFFFFFFFll) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(heads) * D * 2};
+  cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 // 3-D map over a KV cache viewed as [slots = P*PS][HKV][D] with a
@@ -449,13 +468,16 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
 }
 
 int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
-                           void* out, float* lse, int B, int max_q, int max_k, int HQ, int HKV, int D, int causal,
-                           int bf16, float scale, void* stream) {
+                           void* out, float* lse, int B, int max_q, int max_k, int total_q, int total_k, int HQ,
+                           int HKV, int D, int causal, int bf16, float scale, void* stream) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || max_q < 0 || max_k < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad varlen geometry");
   if ((cu_q == nullptr) != (cu_k == nullptr)) return fail(MXFA_ERR_INVALID, "cu_q and cu_k must both be given");
-  if (B == 0 || max_q == 0) return MXFA_OK;
+  if (B == 0 || max_q == 0 || total_q == 0) return MXFA_OK;
+  if (total_q < 0 || total_k <= 0) return fail(MXFA_ERR_INVALID, "total token counts must be positive");
+  if (cu_q == nullptr && (total_q != B * max_q || total_k != B * max_k))
+    return fail(MXFA_ERR_INVALID, "dense layout needs total_q = B*max_q and total_k = B*max_k");
   if (!q || !k || !v || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
   if (HQ > 65535 || B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "grid too large");
@@ -475,19 +497,25 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
   p.GQ = HQ / HKV;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
-  dim3 grid((max_q + kPfRows - 1) / kPfRows, HQ, B);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // TMA maps cover exactly the token rows of q and k/v: boxes reaching past
+  // the last row read zeros instead of memory beyond the tensors
+  CUtensorMap mq, mk, mv;
+  if (!encode_rows_map(&mq, q, D, HQ, total_q, kTcRows) || !encode_rows_map(&mk, k, D, HKV, total_k, kTcKeys) ||
+      !encode_rows_map(&mv, v, D, HKV, total_k, kTcKeys))
+    return fail(MXFA_ERR_UNSUPPORTED, "TMA descriptor encoding failed for the prefill operands");
+  dim3 grid((max_q + kTcRows - 1) / kTcRows, HQ, B);
   auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;
-    kern<<<grid, kPfThreads, smem, st>>>(p);
-    return check_launch("prefill_mma_kernel");
+    kern<<<grid, kTcThreads, smem, st>>>(p, mq, mk, mv);
+    return check_launch("prefill_tc_kernel");
   };
   static std::atomic<unsigned long long> d0{0}, d1{0}, d2{0}, d3{0};
   if (bf16)
-    return D == 128 ? go(prefill_mma_kernel<__nv_bfloat16, 128>, PrefillCfg<128>::kSmemBytes, d0)
-                    : go(prefill_mma_kernel<__nv_bfloat16, 64>, PrefillCfg<64>::kSmemBytes, d1);
-  return D == 128 ? go(prefill_mma_kernel<__half, 128>, PrefillCfg<128>::kSmemBytes, d2)
-                  : go(prefill_mma_kernel<__half, 64>, PrefillCfg<64>::kSmemBytes, d3);
+    return D == 128 ? go(prefill_tc_kernel<__nv_bfloat16, 128>, TcCfg<128>::kSmemBytes, d0)
+                    : go(prefill_tc_kernel<__nv_bfloat16, 64>, TcCfg<64>::kSmemBytes, d1);
+  return D == 128 ? go(prefill_tc_kernel<__half, 128>, TcCfg<128>::kSmemBytes, d2)
+                  : go(prefill_tc_kernel<__half, 64>, TcCfg<64>::kSmemBytes, d3);
 }
 
 }  // extern "C"

@@ -56,7 +56,8 @@ def test_invalid_arguments_return_invalid(lib):
     rc = lib.mxfa_kvcache_attention_launch(None, None, None, None, None, None, None, None, 0, 1, 1, 8, 2, 128, 16,
                                            4, 10, 0, 0, 0, 0, 1, 0.1, None)
     assert rc == _lib.MXFA_ERR_INVALID
-    rc = lib.mxfa_varlen_fwd_launch(None, None, None, None, None, None, None, 1, 4, 4, 8, 2, 80, 1, 1, 0.1, None)
+    rc = lib.mxfa_varlen_fwd_launch(None, None, None, None, None, None, None, 1, 4, 4, 4, 4, 8, 2, 80, 1, 1, 0.1,
+                                    None)
     assert rc == _lib.MXFA_ERR_UNSUPPORTED
 
 

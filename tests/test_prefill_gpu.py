@@ -127,3 +127,28 @@ def test_prefill_config_varlen_sampled_rows(cuda_device):
                 ref = (p / p.sum()) @ vals[: r + 1]
                 err = float(np.max(np.abs(out_h[start + r, h] - ref)))
                 assert err <= 1e-2, f"seq {s} row {r} head {h}: {err:.3e}"
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_no_reads_past_the_packed_tensors(causal, cuda_device):
+    """q/k/v are prefixes of NaN-filled buffers: a read past their last row would poison the output."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_varlen_func
+
+    case = syn.varlen_case(61, q_lens=[37, 130, 3], q_heads=8, kv_heads=2, head_dim=128, dtype="bf16",
+                           causal=causal)
+    tdt = syn.torch_dtype(case.dtype)
+
+    def poisoned(x):
+        big = torch.full((x.shape[0] + 256,) + x.shape[1:], float("nan"), device=cuda_device, dtype=tdt)
+        big[: x.shape[0]] = torch.from_numpy(x).to(cuda_device, tdt)
+        return big[: x.shape[0]]
+
+    q, k, v = poisoned(case.q), poisoned(case.k), poisoned(case.v)
+    cu = torch.from_numpy(case.cu_q).to(cuda_device)
+    out = flash_attn_varlen_func(q, k, v, cu, cu, 130, 130, causal=causal)
+    ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, causal=causal)
+    assert_close_out(host(out), ref, "bf16", f"poisoned tail causal={causal}",
+                     extra=p_rounding_bound("bf16", oracle.attention_varlen(
+                         case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, causal=causal)))
