@@ -9,12 +9,13 @@
 //                       O  += P_j V_j  (M=128, N=D,  K=128; V MN-major)
 //              committing each group to an mbarrier
 //   warps 4-7: softmax, one thread per query row (tensor-memory lane = row):
-//              read S_j with tcgen05.ld, mask, online max in the log2 domain,
-//              write P_j (bf16/fp16) into a double-buffered swizzled shared
-//              tile for the P.V product, rescale O in tensor memory only when
-//              a row max grows by more than 2^8 (rare after the first tiles),
-//              and finally normalise O and store it.
-// Tensor memory: S double buffer (2 x 128 fp32 columns) + O (D columns).
+//              read S_j with tcgen05.ld, mask, keep an online max in the log2
+//              domain, write P_j (bf16/fp16) into tensor memory for the P.V
+//              product (A operand read from TMEM), rescale O in tensor memory
+//              only when a row max grows by more than 2^8 (rare after the
+//              first tiles), and finally normalise O and store it.
+// Tensor memory: S double buffer (2 x 128 fp32 columns) | O (D columns) |
+// P double buffer (2 x 64 columns, two 16-bit values per column).
 // S_{j+1} is issued before P_j is ready, so the tensor pipe computes the next
 // scores while the softmax warps work on the current ones.
 //
@@ -66,6 +67,17 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M rows = lanes, K packed two 16-bit values per column) read
+// straight from tensor memory, so the softmax output never travels through shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -130,27 +142,30 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool b_mn_major)
 constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
 constexpr int kTcKeys = 128;   // keys per tile (MMA N of S, K of P.V)
 constexpr int kTcThreads = 256;
+constexpr int kTcSoftmaxWarps = 4;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when a row max grows by > 2^8
 
 template <int HD>
 struct TcCfg {
   static constexpr int kDBlk = HD / 64;
+  static constexpr int kStages = 3;
   static constexpr int kBlk = 128 * 128;               // one 64-column block of a 128-row tile
   static constexpr int kTile = kDBlk * kBlk;           // Q, K or V tile bytes
-  static constexpr int kPTile = 2 * kBlk;              // P tile: 128 rows x 128 keys
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;                // 2 stages
-  static constexpr int kV = kK + 2 * kTile;            // 2 stages
-  static constexpr int kP = kV + 2 * kTile;            // 2 buffers
-  static constexpr int kBar = kP + 2 * kPTile;
-  static constexpr int kNumBars = 17;
+  static constexpr int kK = kQ + kTile;
+  static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kBar = kV + kStages * kTile;
+  static constexpr int kNumBars = 1 + 4 * kStages + 8;
   static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O
+  static constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O | P0 P1
   static constexpr uint32_t kTmemO = 256;
+  static constexpr uint32_t kTmemP = 384;               // two 64-column P buffers (128 keys, 2 per column)
 };
 
+template <int kStages>
 struct TcBars {
-  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full[2], pv_done[2];
+  uint64_t q_full, k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], s_empty[2], p_full[2], pv_done[2];
 };
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -174,9 +189,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
   using Cfg = TcCfg<HD>;
+  constexpr int NS = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  TcBars* bars = reinterpret_cast<TcBars*>(sm + Cfg::kBar);
+  TcBars<NS>* bars = reinterpret_cast<TcBars<NS>*>(sm + Cfg::kBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kBar + Cfg::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -219,14 +235,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_empty[i], 4);
-      mbar_init(&bars->p_full[i], 4);
+      mbar_init(&bars->s_empty[i], kTcSoftmaxWarps);
+      mbar_init(&bars->p_full[i], kTcSoftmaxWarps);
       mbar_init(&bars->pv_done[i], 1);
     }
     *abort = 0;
@@ -252,7 +270,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int db = 0; db < Cfg::kDBlk; ++db)
         tma_load_3d(sm + Cfg::kQ + db * Cfg::kBlk, &tmq, &bars->q_full, db * 64, h, q_start + q0);
       for (int t = 0; t < nkt && !*abort; ++t) {
-        const int st = t & 1, use = t >> 1;
+        const int st = t % NS, use = t / NS;
         if (use > 0 && !tc_wait(&bars->k_empty[st], (use - 1) & 1, abort)) break;
         mbar_arrive_expect_tx(&bars->k_full[st], Cfg::kTile);
 #pragma unroll
@@ -274,9 +292,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       constexpr uint32_t idesc_o = umma_idesc<T>(kTcRows, HD, true);
       const uint32_t q_base = smem_u32(sm + Cfg::kQ);
       auto issue_s = [&](int t) -> bool {
-        const int sb = t & 1, st = t & 1;
+        const int sb = t & 1, st = t % NS;
         if (t >= 2 && !tc_wait(&bars->s_empty[sb], ((t >> 1) - 1) & 1, abort)) return false;
-        if (!tc_wait(&bars->k_full[st], (t >> 1) & 1, abort)) return false;
+        if (!tc_wait(&bars->k_full[st], (t / NS) & 1, abort)) return false;
         tc_fence_after();
         const uint32_t k_base = smem_u32(sm + Cfg::kK + st * Cfg::kTile);
 #pragma unroll
@@ -293,20 +311,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkt && ok; ++j) {
         if (j + 1 < nkt && !issue_s(j + 1)) break;
-        const int pb = j & 1;
+        const int pb = j & 1, vs = j % NS;
         if (!tc_wait(&bars->p_full[pb], (j >> 1) & 1, abort)) break;
-        if (!tc_wait(&bars->v_full[pb], (j >> 1) & 1, abort)) break;
+        if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t p_base = smem_u32(sm + Cfg::kP + pb * Cfg::kPTile);
-        const uint32_t v_base = smem_u32(sm + Cfg::kV + pb * Cfg::kTile);
+        const uint32_t v_base = smem_u32(sm + Cfg::kV + vs * Cfg::kTile);
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-          const uint64_t pd = smem_desc(p_base + (kk >> 2) * Cfg::kBlk + (kk & 3) * 32, 16, 1024);
           const uint64_t vd = smem_desc(v_base + kk * 16 * 128, Cfg::kBlk, 1024);
-          umma_f16(tmem + Cfg::kTmemO, pd, vd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          // 16 keys = 8 packed columns of the P buffer in tensor memory
+          umma_f16_ts(tmem + Cfg::kTmemO, tmem + Cfg::kTmemP + pb * 64 + kk * 8, vd, idesc_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done[pb]);
-        umma_commit(&bars->v_empty[pb]);
+        umma_commit(&bars->v_empty[vs]);
       }
     }
     __syncwarp();
@@ -338,6 +356,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_empty[sb]);
 
+      // scores into the log2 domain; masked keys become -inf (after scaling, so
+      // a zero scale still gives -inf there and 0 elsewhere)
       const int key0 = j * kTcKeys;
       float mx = -INFINITY;
       if (key0 + kTcKeys <= vis_end) {
@@ -399,13 +419,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
       }
-      uint8_t* pbuf = sm + Cfg::kP + sb * Cfg::kPTile;
-#pragma unroll
-      for (int ch = 0; ch < kTcKeys / 8; ++ch) {
-        const uint4 v = make_uint4(packed[ch * 4], packed[ch * 4 + 1], packed[ch * 4 + 2], packed[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * Cfg::kBlk + swz128(r, ch & 7)) = v;
-      }
-      fence_proxy_async_smem();
+      const uint32_t pt = lane_base + Cfg::kTmemP + sb * 64;
+      tmem_st32(pt, *reinterpret_cast<const uint32_t(*)[32]>(&packed[0]));
+      tmem_st32(pt + 32, *reinterpret_cast<const uint32_t(*)[32]>(&packed[32]));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[sb]);
