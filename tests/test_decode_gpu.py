@@ -239,3 +239,69 @@ def test_long_context_16k_split_vs_oracle(cuda_device):
     ref, ref_lse = oracle_paged(case)[:2]
     assert_close_out(host(out), ref, "bf16", "16k")
     assert_close_lse(host(lse), ref_lse, "16k")
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_qwen3_8b_config_batch16(dt, cuda_device):
+    """Benchmark config 3: Qwen3-8B decode, B=16, Hq=32, Hk=8, D=128, ctx U[256,1280], fp16 and bf16.
+
+    16 sequences x 8 KV heads = 128 units < 148 SMs, so the library plan splits
+    the context; the split partials and the combine are exercised at full size.
+    """
+    from mxflashattn_b200 import backend, flash_attn_with_kvcache
+
+    lengths = syn.qwen3_8b_lengths(8)
+    case = syn.paged_case(88 + (dt == "bf16"), batch=16, q_heads=32, kv_heads=8, head_dim=128, dtype=dt,
+                          page_size=16, lengths=lengths)
+    t = to_device(case, cuda_device)
+    plan = backend.kvcache_plan(16, 1, 32, 8, 128, case.block_table.shape[1] * 16)
+    assert plan[0] > 1, "the 8B batch should be split across SMs"
+    out = flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"], cache_seqlens=t["cache_seqlens"],
+                                  block_table=t["block_table"])
+    assert_close_out(host(out), oracle_paged(case)[0], dt, f"qwen3-8b {dt}")
+
+
+def test_kvcache_call_captures_into_a_cuda_graph(cuda_device):
+    """Append + attention + in-place length update recorded once, replayed twice.
+
+    Nothing in the path synchronises or reads device memory on the host, so
+    the whole call captures; each replay appends the next token and advances
+    cache_seqlens on the device, like vLLM's graph-mode decode step.
+    """
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    case = syn.paged_case(515, batch=4, q_heads=16, kv_heads=4, head_dim=128, dtype="bf16", page_size=16,
+                          lengths=[10, 100, 31, 64], append=2, extra_table_cols=1)
+    t = to_device(case, cuda_device)
+    k_steps = [t["k"][:, i:i + 1].clone() for i in range(2)]
+    v_steps = [t["v"][:, i:i + 1].clone() for i in range(2)]
+    q_in = t["q"].clone()
+    k_in, v_in = k_steps[0].clone(), v_steps[0].clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up on a scratch copy so the capture sees initialised state
+        flash_attn_with_kvcache(q_in, t["k_cache"].clone(), t["v_cache"].clone(), k=k_in, v=v_in,
+                                cache_seqlens=t["cache_seqlens"].clone(), block_table=t["block_table"])
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = flash_attn_with_kvcache(q_in, t["k_cache"], t["v_cache"], k=k_in, v=v_in,
+                                      cache_seqlens=t["cache_seqlens"], block_table=t["block_table"])
+    # capture recorded the work without running it: replay step 1, then step 2
+    kc, vc, sl = case.k_cache.copy(), case.v_cache.copy(), case.cache_seqlens.copy()
+    import oracle
+
+    for i in range(2):
+        k_in.copy_(k_steps[i])
+        v_in.copy_(v_steps[i])
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oracle.attention_kvcache(case.q, kc, vc, cache_seqlens=sl, block_table=case.block_table,
+                                       k=case.k_new[:, i:i + 1], v=case.v_new[:, i:i + 1],
+                                       softmax_scale=case.softmax_scale)
+        assert_close_out(host(out), ref, "bf16", f"graph replay {i}")
+        np.testing.assert_array_equal(t["cache_seqlens"].cpu().numpy(), sl)
+    np.testing.assert_array_equal(host(t["k_cache"]), kc)
+    del graph
