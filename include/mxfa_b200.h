@@ -110,6 +110,24 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
                                   int append_len, int num_splits, int chunk_len, int causal,
                                   int bf16, float scale, void* stream);
 
+/* mxfa_kvcache_attention_launch with the append fused into the same launch:
+ * the append of reference.py:108-122 (what mxfa_kv_append_launch does) plus
+ * the attention over the grown cache, in one kernel.  k_new, v_new
+ * [B, append_len, HKV, D] are written into k_cache / v_cache by the CTA that
+ * reads those positions, then attended to.  seqlens still holds the lengths
+ * before the append and is not modified (advance it with
+ * mxfa_seqlens_add_launch).  Up to 16 query rows per KV head (Sq * GQ <= 16,
+ * every single-token decode); larger shapes return MXFA_ERR_UNSUPPORTED and
+ * need the separate append.  No reference counterpart as one entry point: the
+ * reference appended on the host (reference.py:117-122). */
+int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_cache,
+                                         const int32_t* block_table, const int32_t* seqlens, void* out,
+                                         float* lse, void* workspace, size_t workspace_bytes,
+                                         const void* k_new, const void* v_new, int B, int Sq, int HQ,
+                                         int HKV, int D, int PS, int BTW, int num_pages, int append_len,
+                                         int num_splits, int chunk_len, int causal, int bf16, float scale,
+                                         void* stream);
+
 /* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
  * counterpart in the reference.  It exists for callers that cannot allocate
  * device memory when they run attention (an engine that pre-reserved all GPU

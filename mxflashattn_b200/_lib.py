@@ -42,6 +42,9 @@ SIGNATURES = {
     "mxfa_kvcache_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _f, _vp]),
+    "mxfa_kvcache_append_attention_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _i, _f, _vp]),
     "mxfa_kvcache_attention_noalloc_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "mxfa_kvcache_attention_packed_launch": (

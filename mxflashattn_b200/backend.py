@@ -118,11 +118,14 @@ def kvcache_plan(batch: int, q_len: int, q_heads: int, kv_heads: int, head_dim: 
 
 def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
                       append_len: int = 0, return_lse: bool = False, num_splits: int = 0, chunk_len: int = 0,
-                      out=None):
+                      out=None, k_new=None, v_new=None):
     """Attention of q [B, Sq, HQ, D] over the cached tokens (+ ``append_len``).
 
-    ``cache_seqlens`` holds the lengths before the append; nothing is written
-    to the caches here.  ``num_splits``/``chunk_len`` 0 = library plan.
+    ``cache_seqlens`` holds the lengths before the append.  Without
+    ``k_new``/``v_new`` nothing is written to the caches (the appended rows
+    must already be there); with them the same launch writes those rows into
+    the caches first (``mxfa_kvcache_append_attention_launch``).
+    ``num_splits``/``chunk_len`` 0 = library plan.
     """
     B, Sq, HQ, D = q.shape
     q = _contig(q)
@@ -150,12 +153,31 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
         ws_bytes = int(lib.mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits))
         ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
-        rc = lib.mxfa_kvcache_attention_launch(
-            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), out.data_ptr(),
-            _lib.ptr(lse), _lib.ptr(ws), ws_bytes, B, Sq, HQ, HKV, D, PS, btw, pages, int(append_len),
-            num_splits, chunk_len, int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
-    _lib.check(rc, "mxfa_kvcache_attention_launch")
+        if k_new is None:
+            name = "mxfa_kvcache_attention_launch"
+            rc = lib.mxfa_kvcache_attention_launch(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
+                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, B, Sq, HQ, HKV, D, PS, btw, pages,
+                int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q), float(softmax_scale),
+                _stream(q))
+        else:
+            name = "mxfa_kvcache_append_attention_launch"
+            k_new, v_new = _contig(k_new), _contig(v_new)
+            rc = lib.mxfa_kvcache_append_attention_launch(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
+                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, k_new.data_ptr(), v_new.data_ptr(), B, Sq,
+                HQ, HKV, D, PS, btw, pages, int(k_new.shape[1]), num_splits, chunk_len, int(bool(causal)),
+                _bf16(q), float(softmax_scale), _stream(q))
+    _lib.check(rc, name)
     return (out, lse) if return_lse else out
+
+
+def fused_append_supported(q, k_cache, k) -> bool:
+    """True when one launch can append ``k``/``v`` and attend (up to 16 query rows per KV head)."""
+    B, Sq, HQ, D = q.shape
+    HKV = k_cache.shape[2]
+    return (k is not None and k.shape[1] > 0 and HQ % HKV == 0 and Sq * (HQ // HKV) <= 16
+            and k.dtype == k_cache.dtype)
 
 
 def kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table) -> None:
@@ -199,6 +221,13 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_tabl
             seqlens_add_(cache_seqlens, k.shape[1])
         return torch.empty_like(q)
     append_len = 0
+    if k is not None and fused_append_supported(q, k_cache, k):
+        # decode shapes: the attention kernel writes the new rows itself (one launch fewer)
+        append_len = k.shape[1]
+        out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
+                                append_len=append_len, k_new=k, v_new=v)
+        seqlens_add_(cache_seqlens, append_len)
+        return out
     if k is not None:
         kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
         append_len = k.shape[1]

@@ -264,11 +264,12 @@ int mxfa_kvcache_plan(int B, int Sq, int HQ, int HKV, int D, int max_len, int* n
   return MXFA_OK;
 }
 
-int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void* v_cache,
+static int kvcache_attention_impl(const void* q, const void* k_cache, const void* v_cache,
                                   const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
                                   void* workspace, size_t workspace_bytes, int B, int Sq, int HQ, int HKV, int D,
                                   int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
-                                  int causal, int bf16, float scale, void* stream) {
+                                  int causal, int bf16, float scale, const void* k_new, const void* v_new,
+                                  void* stream) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
@@ -297,6 +298,8 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
   p.append_len = append_len;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
+  p.k_new = k_new;
+  p.v_new = v_new;
   const int max_len = block_table ? BTW * PS : PS;
   if (num_splits <= 0 || chunk_len <= 0) {
     mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
@@ -320,6 +323,34 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
   p.mdws = p.ows + rows * num_splits * D;
   if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
   return run_combine<false>(p.ows, p.mdws, out, nullptr, lse, static_cast<int>(rows), D, num_splits, bf16 != 0, st);
+}
+
+int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
+                                  void* workspace, size_t workspace_bytes, int B, int Sq, int HQ, int HKV, int D,
+                                  int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
+                                  int causal, int bf16, float scale, void* stream) {
+  return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
+                                Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
+                                scale, nullptr, nullptr, stream);
+}
+
+int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_cache,
+                                         const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
+                                         void* workspace, size_t workspace_bytes, const void* k_new,
+                                         const void* v_new, int B, int Sq, int HQ, int HKV, int D, int PS, int BTW,
+                                         int num_pages, int append_len, int num_splits, int chunk_len, int causal,
+                                         int bf16, float scale, void* stream) {
+  if (k_new == nullptr || v_new == nullptr || append_len <= 0)
+    return fail(MXFA_ERR_INVALID, "fused append needs k_new, v_new and append_len > 0");
+  if (HKV <= 0 || HQ % HKV != 0 || Sq * (HQ / HKV) > 16)
+    return fail(MXFA_ERR_UNSUPPORTED, "fused append covers up to 16 query rows per KV head (Sq*GQ=%d)",
+                HKV > 0 ? Sq * (HQ / HKV) : 0);
+  if (!aligned16(k_new) || !aligned16(v_new) || (D * 2) % 16 != 0)
+    return fail(MXFA_ERR_INVALID, "appended rows must be 16-byte aligned");
+  return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes,
+                                B, Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal,
+                                bf16, scale, k_new, v_new, stream);
 }
 
 int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt, const void* sl,

@@ -43,6 +43,10 @@ struct DecodeParams {
   int NP, c_len;         // splits; chunk z covers [z*c_len, (z+1)*c_len)
   int causal;
   float scale_log2;      // softmax_scale * log2(e)
+  // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
+  // written into the cache by the CTA that reads them (one query-row group only).
+  const void* k_new;
+  const void* v_new;
 };
 
 constexpr int kDecConsumerWarps = 4;
@@ -129,6 +133,47 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
   }
   const int tile0 = (lo / kTileTok) * kTileTok;
   const int ntiles = (hi > lo) ? (hi - tile0 + kTileTok - 1) / kTileTok : 0;
+
+  if (p.k_new != nullptr) {
+    // Fused append: this CTA is the only reader of its KV head's positions in
+    // [lo, hi), so it writes the appended rows that fall there itself; the
+    // proxy fence plus the barrier below order these generic stores before
+    // the producer's TMA reads of the same pages.
+    const int old_len = total_len - p.append_len;
+    const int a_lo = max(lo, old_len), a_hi = min(hi, total_len);
+    // positions past the cache's capacity belong to no chunk: report them once
+    const int capacity = p.bt != nullptr ? p.BTW * p.PS : p.PS;
+    if (threadIdx.x == 0 && z == 0 && rg == 0 && total_len > capacity)
+      raise_flag(p.bt != nullptr ? MXFA_FLAG_TABLE_TOO_NARROW : MXFA_FLAG_DENSE_OVERFLOW);
+    constexpr int kChunks = HD / 8;
+    for (int c = threadIdx.x; c < (a_hi - a_lo) * kChunks; c += blockDim.x) {
+      const int pos = a_lo + c / kChunks;
+      const int ch = c % kChunks;
+      const int page = pos / p.PS;
+      int phys = b;
+      if (p.bt != nullptr) {
+        if (page >= p.BTW) {
+          raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+          continue;
+        }
+        phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+      } else if (pos >= p.PS) {
+        raise_flag(MXFA_FLAG_DENSE_OVERFLOW);
+        continue;
+      }
+      if (phys < 0 || phys >= p.P) {
+        raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+        continue;
+      }
+      const size_t src = ((static_cast<size_t>(b) * p.append_len + (pos - old_len)) * p.HKV + kvh) * HD + ch * 8;
+      const size_t dst = ((static_cast<size_t>(phys) * p.PS + pos % p.PS) * p.HKV + kvh) * HD + ch * 8;
+      *reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + dst) =
+          *reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_new) + src);
+      *reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + dst) =
+          *reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_new) + src);
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kSlots; ++s) {
