@@ -102,6 +102,26 @@ bool encode_rows_map(CUtensorMap* map, const void* base, int D, int heads, long 
 
 // 3-D map over a KV cache viewed as [slots = P*PS][HKV][D] with a
 // (64 columns, 1 head, 16 slots) box and 128-byte swizzle.
+// 4-D view of the same cache for whole-tile boxes: dims (64 columns, head,
+// slot row, 64-column block) with byte strides (D*2, HKV*D*2, 128); the box
+// (64, 1, 16, D/64) lands in shared memory as [block][row][128 B], exactly
+// the layout two 3-D boxes produce, in one copy instead of D/64.
+bool encode_kv_map_4d(CUtensorMap* map, const void* base, int D, int HKV, long long slots) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  if (slots <= 0 || slots > 0xFFFFFFFFll) return false;
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(HKV), static_cast<cuuint64_t>(slots),
+                        static_cast<cuuint64_t>(D / 64)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(HKV) * D * 2, 128};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kTileTok), static_cast<cuuint32_t>(D / 64)};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool encode_kv_map(CUtensorMap* map, const void* base, int D, int HKV, long long slots) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return false;
@@ -154,7 +174,9 @@ int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
   bool tma = (p.PS % kTileTok) == 0;
   if (tma) {
     const long long slots = static_cast<long long>(p.P) * p.PS;
-    tma = encode_kv_map(&tk, p.k, D, p.HKV, slots) && encode_kv_map(&tv, p.v, D, p.HKV, slots);
+    p.kv_map_4d = encode_kv_map_4d(&tk, p.k, D, p.HKV, slots) && encode_kv_map_4d(&tv, p.v, D, p.HKV, slots);
+    if (!p.kv_map_4d)
+      tma = encode_kv_map(&tk, p.k, D, p.HKV, slots) && encode_kv_map(&tv, p.v, D, p.HKV, slots);
   }
   if (bf16)
     return D == 128 ? launch_decode_t<__nv_bfloat16, 128>(p, nt, tma, grid, tk, tv, st)

@@ -43,6 +43,7 @@ struct DecodeParams {
   int NP, c_len;         // splits; chunk z covers [z*c_len, (z+1)*c_len)
   int causal;
   float scale_log2;      // softmax_scale * log2(e)
+  int kv_map_4d;         // TMA maps are 4-D: one box holds a whole 16-token K (or V) tile
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -83,6 +84,30 @@ struct DecodeMerge {
   static constexpr int kBytes = kOBytes + 2 * kDecConsumerWarps * kCols * 4;
 };
 
+// Physical slot row (page * PS + offset) of 16-token tile t of sequence b,
+// read from the block table; 0 past the last tile.  A page index past the
+// table or a physical page outside the cache is flagged and redirected (the
+// last table column, or row P*PS which lies past the tensor so TMA fills the
+// box with zeros and reads nothing).
+__device__ __forceinline__ int tile_slot_row(const DecodeParams& p, int b, int tile0, int ntiles, int t) {
+  if (t >= ntiles) return 0;
+  const int pos = tile0 + t * kTileTok;
+  int page = pos / p.PS;
+  int phys = b;
+  if (p.bt != nullptr) {
+    if (page >= p.BTW) {
+      raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+      page = p.BTW - 1;
+    }
+    phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+  }
+  if (phys < 0 || phys >= p.P) {
+    raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+    phys = p.P;
+  }
+  return phys * p.PS + (pos % p.PS);
+}
+
 template <typename T, int HD, int NT, bool kTma>
 __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
@@ -104,26 +129,50 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int b = blockIdx.y;
+  int cached_len;
   if (p.B > 1 && p.B <= kRankMaxBatch) {
-    __shared__ int s_seq;
-    int* lens = reinterpret_cast<int*>(ring);  // ring is not in use yet
-    for (int i = threadIdx.x; i < p.B; i += blockDim.x) lens[i] = p.seqlens[i];
+    // Rank every sequence by length (ties by index) and take the one whose
+    // rank is this block's y.  Each sequence gets one packed key -- length in
+    // the high bits, reversed index in the low 9 -- so keys are unique and a
+    // rank is one compare per pair; keys are padded to a multiple of 4 with
+    // -1 and read four at a time.  The chosen length comes back with the
+    // index so no second global read sits on the start-up path.
+    __shared__ int s_seq, s_len;
+    int* keys = reinterpret_cast<int*>(ring);  // ring is not in use yet
+    int* lens = keys + kRankMaxBatch;
+    const int bp = (p.B + 3) & ~3;
+    for (int i = threadIdx.x; i < bp; i += blockDim.x) {
+      int key = -1;
+      if (i < p.B) {
+        const int len = p.seqlens[i];
+        lens[i] = len;
+        key = (min(max(len, 0), (1 << 22) - 1) << 9) | (kRankMaxBatch - 1 - i);
+      }
+      keys[i] = key;
+    }
     __syncthreads();
     const int want = blockIdx.y;
+    const int4* keys4 = reinterpret_cast<const int4*>(keys);
     for (int i = threadIdx.x; i < p.B; i += blockDim.x) {
-      const int li = lens[i];
+      const int ki = keys[i];
       int rank = 0;
-      for (int j = 0; j < p.B; ++j) {
-        const int lj = lens[j];
-        rank += (lj > li) || (lj == li && j < i);
+      for (int j4 = 0; j4 < bp / 4; ++j4) {
+        const int4 v = keys4[j4];
+        rank += (v.x > ki) + (v.y > ki) + (v.z > ki) + (v.w > ki);
       }
-      if (rank == want) s_seq = i;
+      if (rank == want) {
+        s_seq = i;
+        s_len = lens[i];
+      }
     }
     __syncthreads();
     b = s_seq;
+    cached_len = s_len;
+  } else {
+    cached_len = p.seqlens[b];
   }
 
-  const int total_len = p.seqlens[b] + p.append_len;
+  const int total_len = cached_len + p.append_len;
   // split mode (partials written for a combine) whenever a workspace is given;
   // chunk z then covers [z*c_len, (z+1)*c_len) exactly as the reference's split
   int lo = 0, hi = total_len;
@@ -133,6 +182,11 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
   }
   const int tile0 = (lo / kTileTok) * kTileTok;
   const int ntiles = (hi > lo) ? (hi - tile0 + kTileTok - 1) / kTileTok : 0;
+
+  // The producer's first block-table reads go out now, so their latency
+  // overlaps the barrier set-up below (only the TMA path uses them).
+  int first_rows = 0;
+  if (kTma && warp == kDecConsumerWarps) first_rows = tile_slot_row(p, b, tile0, ntiles, lane);
 
   if (p.k_new != nullptr) {
     // Fused append: this CTA is the only reader of its KV head's positions in
@@ -194,27 +248,11 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
         prefetch_tensormap(&tmv);
       }
       int abort = 0;
+      int issued = 0;  // lane 0: tiles whose copies were started
       for (int base = 0; base < ntiles && !abort; base += 32) {
-        // lane j resolves the physical slot row of tile base + j (one load per lane)
-        const int t = base + lane;
-        int slot_row = 0;
-        if (t < ntiles) {
-          const int pos = tile0 + t * kTileTok;
-          int page = pos / p.PS;
-          int phys = b;
-          if (p.bt != nullptr) {
-            if (page >= p.BTW) {
-              raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
-              page = p.BTW - 1;
-            }
-            phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
-          }
-          if (phys < 0 || phys >= p.P) {
-            raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
-            phys = p.P;  // box lies past the tensor: TMA fills zeros, reads nothing
-          }
-          slot_row = phys * p.PS + (pos % p.PS);
-        }
+        // lane j holds the physical slot row of tile base + j (the first 32
+        // were resolved before the start-up barrier)
+        const int slot_row = base == 0 ? first_rows : tile_slot_row(p, b, tile0, ntiles, base + lane);
         const int n = min(32, ntiles - base);
         for (int j = 0; j < n; ++j) {
           const int row = __shfl_sync(0xffffffffu, slot_row, j);
@@ -225,13 +263,20 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
             if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
               abort = 1;
             } else {
+              issued = tt + 1;
               mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kTileBytes);
               uint8_t* kd = ring + slot * Cfg::kSlotBytes;
               uint8_t* vd = kd + Cfg::kTileBytes;
+              if (p.kv_map_4d) {
+                // one box per tensor: (64 columns, head, 16 rows, column block)
+                tma_load_4d(kd, &tmk, &full[slot], 0, kvh, row, 0);
+                tma_load_4d(vd, &tmv, &full[slot], 0, kvh, row, 0);
+              } else {
 #pragma unroll
-              for (int db = 0; db < Cfg::kDBlk; ++db) {
-                tma_load_3d(kd + db * Cfg::kBlkBytes, &tmk, &full[slot], db * 64, kvh, row);
-                tma_load_3d(vd + db * Cfg::kBlkBytes, &tmv, &full[slot], db * 64, kvh, row);
+                for (int db = 0; db < Cfg::kDBlk; ++db) {
+                  tma_load_3d(kd + db * Cfg::kBlkBytes, &tmk, &full[slot], db * 64, kvh, row);
+                  tma_load_3d(vd + db * Cfg::kBlkBytes, &tmv, &full[slot], db * 64, kvh, row);
+                }
               }
             }
           }
@@ -239,42 +284,60 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
           if (abort) break;
         }
       }
+      // every copy issued must land before the CTA exits: wait (bounded) for
+      // the last phase of each slot used
+      if (lane == 0)
+        for (int tt = max(issued - Cfg::kSlots, 0); tt < issued; ++tt)
+          mbar_wait(&full[tt % Cfg::kSlots], (tt / Cfg::kSlots) & 1);
     } else {
-      constexpr int kChunks = kTileTok * (HD / 8);  // 16-byte chunks per tile per tensor
+      constexpr int kRowChunks = HD / 8;               // 16-byte chunks per row
+      constexpr int kChunks = kTileTok * kRowChunks;  // per tile per tensor (a multiple of 32)
       for (int t = 0; t < ntiles; ++t) {
         const int slot = t % Cfg::kSlots;
         const int use = t / Cfg::kSlots;
-        if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) break;
+        const bool ready = use == 0 || mbar_wait(&empty[slot], (use - 1) & 1);
+        if (!__all_sync(0xffffffffu, ready)) break;  // every lane leaves together
         uint8_t* kd = ring + slot * Cfg::kSlotBytes;
         uint8_t* vd = kd + Cfg::kTileBytes;
         const int pos0 = tile0 + t * kTileTok;
-#pragma unroll 2
-        for (int c = lane; c < kChunks; c += 32) {
-          const int r = c / (HD / 8);
-          const int ch = c % (HD / 8);
-          const int pos = pos0 + r;
-          if (pos < lo || pos >= hi) continue;  // left stale; consumers mask / zero it
-          const int page = pos / p.PS;
-          int phys = b;
-          if (p.bt != nullptr) {
-            if (page >= p.BTW) {
-              raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
-              continue;
+        // lane r < 16 resolves row r's element offset once (-1: outside [lo, hi)
+        // or not mapped; the slot row is left stale and consumers mask / zero it)
+        long long roff = -1;
+        if (lane < kTileTok) {
+          const int pos = pos0 + lane;
+          if (pos >= lo && pos < hi) {
+            const int page = pos / p.PS;
+            int phys = b;
+            bool mapped = true;
+            if (p.bt != nullptr) {
+              if (page >= p.BTW) {
+                raise_flag(MXFA_FLAG_TABLE_TOO_NARROW);
+                mapped = false;
+              } else {
+                phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+              }
             }
-            phys = p.bt[static_cast<size_t>(b) * p.BTW + page];
+            if (mapped && (phys < 0 || phys >= p.P)) {
+              raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
+              mapped = false;
+            }
+            if (mapped)
+              roff = ((static_cast<long long>(phys) * p.PS + (pos % p.PS)) * p.HKV + kvh) * HD;
           }
-          if (phys < 0 || phys >= p.P) {
-            raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
-            continue;
-          }
-          const size_t off =
-              ((static_cast<size_t>(phys) * p.PS + (pos % p.PS)) * p.HKV + kvh) * HD + ch * 8;
+        }
+#pragma unroll 4
+        for (int c = lane; c < kChunks; c += 32) {
+          const int r = c / kRowChunks;
+          const int ch = c % kRowChunks;
+          const long long off = __shfl_sync(0xffffffffu, roff, r);
+          if (off < 0) continue;
           const uint32_t so = (ch >> 3) * Cfg::kBlkBytes + swz128(r, ch & 7);
-          cp_async_16(kd + so, kc + off);
-          cp_async_16(vd + so, vc + off);
+          cp_async_16(kd + so, kc + off + ch * 8);
+          cp_async_16(vd + so, vc + off + ch * 8);
         }
         cp_async_mbar_arrive_noinc(&full[slot]);
       }
+      cp_async_wait_all();  // this lane's copies have landed before it exits
     }
     return;
   }
