@@ -106,6 +106,36 @@ bool encode_rows_map(CUtensorMap* map, const void* base, int D, int heads, long 
 // slot row, 64-column block) with byte strides (D*2, HKV*D*2, 128); the box
 // (64, 1, 16, D/64) lands in shared memory as [block][row][128 B], exactly
 // the layout two 3-D boxes produce, in one copy instead of D/64.
+// 5-D view over BOTH caches for one box per K+V tile: the 4-D view above
+// plus a fifth dimension of extent 2 whose stride is the byte distance from
+// the lower of the two caches to the higher.  The box lands as [K|V][block]
+// [row][128 B] (V first when V lies below K, reported through *swap).  Any
+// in-range coordinate addresses an element of K or V; rows past the caches
+// are zero-filled without a read, as with the other maps.
+bool encode_kv_map_5d(CUtensorMap* map, const void* k, const void* v, int D, int HKV, long long slots,
+                      int* swap) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const uintptr_t ka = reinterpret_cast<uintptr_t>(k), va = reinterpret_cast<uintptr_t>(v);
+  if (((ka | va) & 15) != 0 || ka == va) return false;
+  if (slots <= 0 || slots > 0xFFFFFFFFll) return false;
+  const uintptr_t lo = ka < va ? ka : va;
+  const unsigned long long dist = ka < va ? va - ka : ka - va;
+  if (dist >= (1ull << 40)) return false;  // tensor-map stride limit
+  cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(HKV), static_cast<cuuint64_t>(slots),
+                        static_cast<cuuint64_t>(D / 64), 2};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(HKV) * D * 2, 128,
+                           static_cast<cuuint64_t>(dist)};
+  cuuint32_t box[5] = {64, 1, static_cast<cuuint32_t>(kTileTok), static_cast<cuuint32_t>(D / 64), 2};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5, reinterpret_cast<void*>(lo), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  *swap = va < ka ? 1 : 0;
+  return true;
+}
+
 bool encode_kv_map_4d(CUtensorMap* map, const void* base, int D, int HKV, long long slots) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return false;
@@ -174,9 +204,18 @@ int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
   bool tma = (p.PS % kTileTok) == 0;
   if (tma) {
     const long long slots = static_cast<long long>(p.P) * p.PS;
-    p.kv_map_4d = encode_kv_map_4d(&tk, p.k, D, p.HKV, slots) && encode_kv_map_4d(&tv, p.v, D, p.HKV, slots);
-    if (!p.kv_map_4d)
+    // fewest copies per tile that the driver accepts: K+V in one box, else
+    // one box per cache, else one per 64-column block
+    int swap = 0;
+    if (encode_kv_map_5d(&tk, p.k, p.v, D, p.HKV, slots, &swap)) {
+      p.kv_map = 5;
+      p.kv_swap = swap;
+    } else if (encode_kv_map_4d(&tk, p.k, D, p.HKV, slots) && encode_kv_map_4d(&tv, p.v, D, p.HKV, slots)) {
+      p.kv_map = 4;
+    } else {
+      p.kv_map = 3;
       tma = encode_kv_map(&tk, p.k, D, p.HKV, slots) && encode_kv_map(&tv, p.v, D, p.HKV, slots);
+    }
   }
   if (bf16)
     return D == 128 ? launch_decode_t<__nv_bfloat16, 128>(p, nt, tma, grid, tk, tv, st)

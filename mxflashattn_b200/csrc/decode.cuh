@@ -43,7 +43,11 @@ struct DecodeParams {
   int NP, c_len;         // splits; chunk z covers [z*c_len, (z+1)*c_len)
   int causal;
   float scale_log2;      // softmax_scale * log2(e)
-  int kv_map_4d;         // TMA maps are 4-D: one box holds a whole 16-token K (or V) tile
+  // TMA map shape: 3 = one box per 64-column block of K or V; 4 = one box per
+  // K or V tile; 5 = one box for the whole K+V tile (tmk then spans both
+  // caches, V at the lower address first when kv_swap)
+  int kv_map;
+  int kv_swap;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -267,7 +271,10 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
               mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kTileBytes);
               uint8_t* kd = ring + slot * Cfg::kSlotBytes;
               uint8_t* vd = kd + Cfg::kTileBytes;
-              if (p.kv_map_4d) {
+              if (p.kv_map == 5) {
+                // one box: (64 columns, head, 16 rows, column block, K|V)
+                tma_load_5d(ring + slot * Cfg::kSlotBytes, &tmk, &full[slot], 0, kvh, row, 0, 0);
+              } else if (p.kv_map == 4) {
                 // one box per tensor: (64 columns, head, 16 rows, column block)
                 tma_load_4d(kd, &tmk, &full[slot], 0, kvh, row, 0);
                 tma_load_4d(vd, &tmv, &full[slot], 0, kvh, row, 0);
@@ -393,8 +400,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
   for (int t = warp; t < ntiles; t += kDecConsumerWarps) {
     const int slot = t % Cfg::kSlots;
     if (!mbar_wait(&full[slot], (t / Cfg::kSlots) & 1)) break;
-    uint8_t* kd = ring + slot * Cfg::kSlotBytes;
-    uint8_t* vd = kd + Cfg::kTileBytes;
+    uint8_t* kd = ring + slot * Cfg::kSlotBytes + (p.kv_swap ? Cfg::kTileBytes : 0);
+    uint8_t* vd = ring + slot * Cfg::kSlotBytes + (p.kv_swap ? 0 : Cfg::kTileBytes);
     const int pos0 = tile0 + t * kTileTok;
     const bool partial = (pos0 < lo) || (pos0 + kTileTok > hi);
     if (partial) {

@@ -305,3 +305,31 @@ def test_kvcache_call_captures_into_a_cuda_graph(cuda_device):
         np.testing.assert_array_equal(t["cache_seqlens"].cpu().numpy(), sl)
     np.testing.assert_array_equal(host(t["k_cache"]), kc)
     del graph
+
+
+@pytest.mark.parametrize("v_first", [False, True])
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_kv_caches_in_either_address_order(v_first, head_dim, cuda_device):
+    """K and V as the two halves of one [2, P, PS, HKV, D] buffer, in either order.
+
+    The TMA path loads a whole K+V tile with one box whose outer dimension is
+    the distance between the caches, so both orders (V above or below K) must
+    give the oracle's result.
+    """
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    case = syn.paged_case(808 + head_dim + int(v_first), batch=3, q_heads=8, kv_heads=2, head_dim=head_dim,
+                          dtype="bf16", page_size=16, lengths=[7, 300, 129])
+    t = to_device(case, cuda_device)
+    kv = torch.empty((2,) + tuple(t["k_cache"].shape), device=cuda_device, dtype=t["k_cache"].dtype)
+    k_half, v_half = (kv[1], kv[0]) if v_first else (kv[0], kv[1])
+    k_half.copy_(t["k_cache"])
+    v_half.copy_(t["v_cache"])
+    assert (v_half.data_ptr() < k_half.data_ptr()) == v_first
+    out = backend.kvcache_attention(t["q"], k_half, v_half, t["cache_seqlens"], t["block_table"],
+                                    case.softmax_scale, False)
+    torch.cuda.synchronize()
+    assert_close_out(host(out), oracle_paged(case)[0], "bf16", f"v_first={v_first} D={head_dim}")
+    _no_device_flags()
