@@ -110,6 +110,27 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
                                   int append_len, int num_splits, int chunk_len, int causal,
                                   int bf16, float scale, void* stream);
 
+/* Counter array for the single-launch split path: one unsigned per
+ * (sequence, KV head, query-row group), i.e. B * HKV * ceil(Sq*GQ / g) * 4
+ * bytes with g = 8 for Sq*GQ <= 8, else 16.  The caller zeroes it once after
+ * allocating; every launch leaves it zero again. */
+size_t mxfa_split_counter_bytes(int B, int Sq, int HQ, int HKV);
+
+/* mxfa_kvcache_attention_launch in ONE kernel launch when the plan splits:
+ * each split CTA publishes its partial state, counts itself on its unit's
+ * counter, and the last one merges the unit's partials into out / lse (the
+ * combine of m1_kernel.cpp:862-888 run inside the decode launch, removing
+ * the second launch of m1_kernel.cpp:1000).  `counters` (see
+ * mxfa_split_counter_bytes) must be zero on entry and is zero again when the
+ * launch completes; launches that share a counter array must be ordered (one
+ * stream, or events).  Unsplit plans ignore it. */
+int mxfa_kvcache_attention_counted_launch(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_table, const int32_t* seqlens, void* out,
+                                          float* lse, void* workspace, size_t workspace_bytes,
+                                          unsigned int* counters, int B, int Sq, int HQ, int HKV, int D, int PS,
+                                          int BTW, int num_pages, int append_len, int num_splits,
+                                          int chunk_len, int causal, int bf16, float scale, void* stream);
+
 /* mxfa_kvcache_attention_launch with the append fused into the same launch:
  * the append of reference.py:108-122 (what mxfa_kv_append_launch does) plus
  * the attention over the grown cache, in one kernel.  k_new, v_new
@@ -118,15 +139,17 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
  * before the append and is not modified (advance it with
  * mxfa_seqlens_add_launch).  Up to 16 query rows per KV head (Sq * GQ <= 16,
  * every single-token decode); larger shapes return MXFA_ERR_UNSUPPORTED and
- * need the separate append.  No reference counterpart as one entry point: the
- * reference appended on the host (reference.py:117-122). */
+ * need the separate append.  `counters` as in
+ * mxfa_kvcache_attention_counted_launch, or NULL for a separate combine
+ * launch.  No reference counterpart as one entry point: the reference
+ * appended on the host (reference.py:117-122). */
 int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_cache,
                                          const int32_t* block_table, const int32_t* seqlens, void* out,
                                          float* lse, void* workspace, size_t workspace_bytes,
-                                         const void* k_new, const void* v_new, int B, int Sq, int HQ,
-                                         int HKV, int D, int PS, int BTW, int num_pages, int append_len,
-                                         int num_splits, int chunk_len, int causal, int bf16, float scale,
-                                         void* stream);
+                                         unsigned int* counters, const void* k_new, const void* v_new, int B,
+                                         int Sq, int HQ, int HKV, int D, int PS, int BTW, int num_pages,
+                                         int append_len, int num_splits, int chunk_len, int causal, int bf16,
+                                         float scale, void* stream);
 
 /* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
  * counterpart in the reference.  It exists for callers that cannot allocate

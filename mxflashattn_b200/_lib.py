@@ -42,9 +42,13 @@ SIGNATURES = {
     "mxfa_kvcache_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _f, _vp]),
+    "mxfa_split_counter_bytes": (_sz, [_i, _i, _i, _i]),
+    "mxfa_kvcache_attention_counted_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _f, _vp]),
     "mxfa_kvcache_append_attention_launch": (
-        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
-             _i, _i, _f, _vp]),
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _i, _i, _f, _vp]),
     "mxfa_kvcache_attention_noalloc_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "mxfa_kvcache_attention_packed_launch": (

@@ -116,16 +116,35 @@ def kvcache_plan(batch: int, q_len: int, q_heads: int, kv_heads: int, head_dim: 
     return plan
 
 
+_COUNTERS: dict[tuple, "torch.Tensor"] = {}
+
+
+def split_counters(device, stream_handle: int, nbytes: int):
+    """Zeroed counter array for single-launch splits on one (device, stream).
+
+    Every counted launch leaves its counters at zero again, so one array per
+    stream is reused by all launches ordered on that stream; it only grows.
+    """
+    key = (device, stream_handle)
+    buf = _COUNTERS.get(key)
+    n = max(nbytes // 4, 1)
+    if buf is None or buf.numel() < n:
+        buf = _COUNTERS[key] = torch.zeros((max(n, 4096),), device=device, dtype=torch.int32)
+    return buf
+
+
 def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
                       append_len: int = 0, return_lse: bool = False, num_splits: int = 0, chunk_len: int = 0,
-                      out=None, k_new=None, v_new=None):
+                      out=None, k_new=None, v_new=None, single_launch: bool = True):
     """Attention of q [B, Sq, HQ, D] over the cached tokens (+ ``append_len``).
 
     ``cache_seqlens`` holds the lengths before the append.  Without
     ``k_new``/``v_new`` nothing is written to the caches (the appended rows
     must already be there); with them the same launch writes those rows into
     the caches first (``mxfa_kvcache_append_attention_launch``).
-    ``num_splits``/``chunk_len`` 0 = library plan.
+    ``num_splits``/``chunk_len`` 0 = library plan.  A split plan runs as one
+    launch (the last split CTA of each unit merges) unless ``single_launch``
+    is False, which keeps the separate combine kernel.
     """
     B, Sq, HQ, D = q.shape
     q = _contig(q)
@@ -153,21 +172,33 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
         ws_bytes = int(lib.mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits))
         ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
+        stream = _stream(q)
+        counters = None
+        if num_splits > 1 and single_launch:
+            counters = split_counters(q.device, stream, int(lib.mxfa_split_counter_bytes(B, Sq, HQ, HKV)))
         if k_new is None:
-            name = "mxfa_kvcache_attention_launch"
-            rc = lib.mxfa_kvcache_attention_launch(
-                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
-                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, B, Sq, HQ, HKV, D, PS, btw, pages,
-                int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q), float(softmax_scale),
-                _stream(q))
+            if counters is None:
+                name = "mxfa_kvcache_attention_launch"
+                rc = lib.mxfa_kvcache_attention_launch(
+                    q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
+                    out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, B, Sq, HQ, HKV, D, PS, btw, pages,
+                    int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q), float(softmax_scale),
+                    stream)
+            else:
+                name = "mxfa_kvcache_attention_counted_launch"
+                rc = lib.mxfa_kvcache_attention_counted_launch(
+                    q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
+                    out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, counters.data_ptr(), B, Sq, HQ, HKV,
+                    D, PS, btw, pages, int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q),
+                    float(softmax_scale), stream)
         else:
             name = "mxfa_kvcache_append_attention_launch"
             k_new, v_new = _contig(k_new), _contig(v_new)
             rc = lib.mxfa_kvcache_append_attention_launch(
                 q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
-                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, k_new.data_ptr(), v_new.data_ptr(), B, Sq,
-                HQ, HKV, D, PS, btw, pages, int(k_new.shape[1]), num_splits, chunk_len, int(bool(causal)),
-                _bf16(q), float(softmax_scale), _stream(q))
+                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, _lib.ptr(counters), k_new.data_ptr(),
+                v_new.data_ptr(), B, Sq, HQ, HKV, D, PS, btw, pages, int(k_new.shape[1]), num_splits, chunk_len,
+                int(bool(causal)), _bf16(q), float(softmax_scale), stream)
     _lib.check(rc, name)
     return (out, lse) if return_lse else out
 

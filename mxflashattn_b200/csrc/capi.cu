@@ -330,7 +330,7 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
                                   void* workspace, size_t workspace_bytes, int B, int Sq, int HQ, int HKV, int D,
                                   int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
                                   int causal, int bf16, float scale, const void* k_new, const void* v_new,
-                                  void* stream) {
+                                  unsigned* counters, void* stream) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
@@ -382,8 +382,34 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   p.c_len = chunk_len;
   p.ows = static_cast<float*>(workspace);
   p.mdws = p.ows + rows * num_splits * D;
+  if (counters != nullptr) {
+    // one launch: the last split CTA of every unit merges the partials
+    if (reinterpret_cast<uintptr_t>(counters) & 3) return fail(MXFA_ERR_INVALID, "counters must be 4-byte aligned");
+    p.counters = counters;
+    return run_decode(p, D, bf16 != 0, st);
+  }
   if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
   return run_combine<false>(p.ows, p.mdws, out, nullptr, lse, static_cast<int>(rows), D, num_splits, bf16 != 0, st);
+}
+
+size_t mxfa_split_counter_bytes(int B, int Sq, int HQ, int HKV) {
+  if (B <= 0 || Sq <= 0 || HKV <= 0 || HQ <= 0 || HQ % HKV != 0) return 0;
+  const int rows_kv = Sq * (HQ / HKV);
+  const int nt = rows_kv <= 8 ? 1 : 2;
+  const long long groups = (rows_kv + 8 * nt - 1) / (8 * nt);
+  return static_cast<size_t>(B) * HKV * groups * sizeof(unsigned);
+}
+
+int mxfa_kvcache_attention_counted_launch(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
+                                          void* workspace, size_t workspace_bytes, unsigned* counters, int B, int Sq,
+                                          int HQ, int HKV, int D, int PS, int BTW, int num_pages, int append_len,
+                                          int num_splits, int chunk_len, int causal, int bf16, float scale,
+                                          void* stream) {
+  if (counters == nullptr) return fail(MXFA_ERR_INVALID, "counters is NULL");
+  return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
+                                Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
+                                scale, nullptr, nullptr, counters, stream);
 }
 
 int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void* v_cache,
@@ -393,13 +419,13 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
                                   int causal, int bf16, float scale, void* stream) {
   return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
                                 Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
-                                scale, nullptr, nullptr, stream);
+                                scale, nullptr, nullptr, nullptr, stream);
 }
 
 int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_cache,
                                          const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
-                                         void* workspace, size_t workspace_bytes, const void* k_new,
-                                         const void* v_new, int B, int Sq, int HQ, int HKV, int D, int PS, int BTW,
+                                         void* workspace, size_t workspace_bytes, unsigned* counters,
+                                         const void* k_new, const void* v_new, int B, int Sq, int HQ, int HKV, int D, int PS, int BTW,
                                          int num_pages, int append_len, int num_splits, int chunk_len, int causal,
                                          int bf16, float scale, void* stream) {
   if (k_new == nullptr || v_new == nullptr || append_len <= 0)
@@ -411,7 +437,7 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
     return fail(MXFA_ERR_INVALID, "appended rows must be 16-byte aligned");
   return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes,
                                 B, Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal,
-                                bf16, scale, k_new, v_new, stream);
+                                bf16, scale, k_new, v_new, counters, stream);
 }
 
 int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt, const void* sl,

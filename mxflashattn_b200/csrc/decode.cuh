@@ -48,6 +48,11 @@ struct DecodeParams {
   // caches, V at the lower address first when kv_swap)
   int kv_map;
   int kv_swap;
+  // Single-launch split (optional, split mode only): one counter per
+  // (sequence, KV head, row group), zero on entry.  The last of the NP
+  // split CTAs of a unit merges the unit's partials into out / lse and
+  // resets its counter to zero.
+  unsigned* counters;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -110,6 +115,73 @@ __device__ __forceinline__ int tile_slot_row(const DecodeParams& p, int b, int t
     phys = p.P;
   }
   return phys * p.PS + (pos % p.PS);
+}
+
+// Merge the NP split partials of query row r (one warp; lanes own HD/32
+// contiguous columns): M = max m_z, L = sum d_z 2^(m_z - M), O = sum o_z
+// 2^(m_z - M) / L -- the merge algebra of the reference combine
+// (csrc_native/m1_kernel.cpp:862-888), evaluated in two passes so no load
+// waits on the previous split: the lanes first reduce M and L over the
+// splits, then the weighted sum runs with several partial rows in flight.
+// Partials are read past L1 (__ldcg) so a merge may run in the launch that
+// wrote them.
+template <typename T, int HD>
+__device__ __forceinline__ void merge_split_row(const float* ows, const float* mdws, int r, int NP, int lane,
+                                                T* out, float* out_f32, float* lse) {
+  constexpr int kPer = HD / 32;
+  const float* md = mdws + static_cast<size_t>(r) * NP * 2;
+  float M = -INFINITY;
+  for (int pz = lane; pz < NP; pz += 32) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+    if (v.x > -INFINITY && v.y > 0.f) M = fmaxf(M, v.x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (int pz = lane; pz < NP; pz += 32) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+      if (v.x > -INFINITY && v.y > 0.f) L += v.y * fast_exp2(v.x - M);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  if (M != -INFINITY) {
+    const float* src = ows + static_cast<size_t>(r) * NP * HD + lane * kPer;
+    // loads are unconditional (every split's row is in bounds) so the
+    // unrolled iterations issue them back to back; empty or invalid splits
+    // are dropped by a select, never by multiplying their (unread) values
+#pragma unroll 8
+    for (int pz = 0; pz < NP; ++pz) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+      float o[kPer];
+      if constexpr (kPer == 4) {
+        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(pz) * HD));
+        o[0] = o4.x; o[1] = o4.y; o[2] = o4.z; o[3] = o4.w;
+      } else {
+        const float2 o2 = __ldcg(reinterpret_cast<const float2*>(src + static_cast<size_t>(pz) * HD));
+        o[0] = o2.x; o[1] = o2.y;
+      }
+      const bool valid = v.x > -INFINITY && v.y > 0.f;
+      const float w = fast_exp2(v.x - M);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) acc[j] = valid ? fmaf(w, o[j], acc[j]) : acc[j];
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (out != nullptr) {
+    T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
+#pragma unroll
+    for (int j = 0; j < kPer; j += 2) *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
+  }
+  if (out_f32 != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) out_f32[static_cast<size_t>(r) * HD + lane * kPer + j] = acc[j] * inv;
+  }
+  if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
 }
 
 template <typename T, int HD, int NT, bool kTma>
@@ -600,6 +672,29 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
       if (d4 == 0 && p.lse != nullptr) p.lse[R] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
     }
   }
+
+  if (p.counters != nullptr && p.ows != nullptr) {
+    // Single-launch split: publish this chunk's partials, count it, and let
+    // the last chunk of the unit merge all of them.
+    __shared__ int s_last;
+    __threadfence();
+    named_barrier_sync(1, kDecConsumerWarps * 32);
+    unsigned* counter = p.counters + static_cast<size_t>(b) * gridDim.x + blockIdx.x;
+    if (tid == 0) s_last = atomicAdd(counter, 1u) == gridDim.z - 1;
+    named_barrier_sync(1, kDecConsumerWarps * 32);
+    if (s_last) {
+      __threadfence();
+      for (int col = warp; col < Mg::kCols; col += kDecConsumerWarps) {
+        const int rr = row_base + col;
+        if (rr >= rows_total) break;
+        const int i = rr / p.GQ;
+        const int h = kvh * p.GQ + rr % p.GQ;
+        const int R = (b * p.Sq + i) * p.HQ + h;
+        merge_split_row<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
+      }
+      if (tid == 0) *counter = 0u;  // ready for the next launch on this stream
+    }
+  }
 }
 
 // --------------------------------------------------------------- combine
@@ -619,6 +714,10 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const float* __restr
   const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
+  if constexpr (!kPackedLse && !kPackedOut) {
+    merge_split_row<T, HD>(ows, mdws, r, NP, lane, out, out_f32, lse);
+    return;
+  }
   float M = -INFINITY, L = 0.f;
   float acc[kPer];
 #pragma unroll

@@ -128,6 +128,6 @@ def test_fused_append_rejects_more_than_16_rows(cuda_device):
     out = torch.empty_like(q)
     rc = lib.mxfa_kvcache_append_attention_launch(
         q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), sl.data_ptr(), out.data_ptr(), None, None, 0,
-        kn.data_ptr(), kn.data_ptr(), B, Sq, HQ, HKV, D, PS, 2, 2, Sq, 1, 32, 1, 1, ctypes.c_float(0.125), None)
+        None, kn.data_ptr(), kn.data_ptr(), B, Sq, HQ, HKV, D, PS, 2, 2, Sq, 1, 32, 1, 1, ctypes.c_float(0.125), None)
     assert rc == -1  # MXFA_ERR_UNSUPPORTED
     assert "16 query rows" in _lib.last_error()
