@@ -131,6 +131,23 @@ int mxfa_kvcache_attention_counted_launch(const void* q, const void* k_cache, co
                                           int BTW, int num_pages, int append_len, int num_splits,
                                           int chunk_len, int causal, int bf16, float scale, void* stream);
 
+/* mxfa_kvcache_attention_counted_launch over e4m3 caches (FP8 KV, half the
+ * decode bytes).  k_cache / v_cache hold float8_e4m3fn [.., PS, HKV, 128]
+ * (head dim 128 only); the attended values are k_cache * k_scale and
+ * v_cache * v_scale, both positive and finite.  q and out are bf16 (bf16=1)
+ * or fp16.  Tiles are widened to f16 exactly and both products run in f16 on
+ * the tensor cores, so q must stay within the f16 range.  `counters` may be
+ * NULL (separate combine launch when the plan splits).  No reference
+ * counterpart: FP8 KV was planned in docs/V1.5_OPTIMIZATION_PLAN.md:583-670
+ * of the reference and never built there. */
+int mxfa_kvcache_attention_fp8_launch(const void* q, const void* k_cache, const void* v_cache,
+                                      const int32_t* block_table, const int32_t* seqlens, void* out,
+                                      float* lse, void* workspace, size_t workspace_bytes,
+                                      unsigned int* counters, int B, int Sq, int HQ, int HKV, int D, int PS,
+                                      int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
+                                      int causal, int bf16, float scale, float k_scale, float v_scale,
+                                      void* stream);
+
 /* mxfa_kvcache_attention_launch with the append fused into the same launch:
  * the append of reference.py:108-122 (what mxfa_kv_append_launch does) plus
  * the attention over the grown cache, in one kernel.  k_new, v_new

@@ -46,6 +46,9 @@ SIGNATURES = {
     "mxfa_kvcache_attention_counted_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _f, _vp]),
+    "mxfa_kvcache_attention_fp8_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _f, _f, _f, _vp]),
     "mxfa_kvcache_append_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _i, _i, _f, _vp]),

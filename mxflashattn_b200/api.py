@@ -8,6 +8,7 @@ sm_100a CUDA library.
 
 from __future__ import annotations
 
+import math
 import os
 
 import torch
@@ -134,11 +135,19 @@ def flash_attn_with_kvcache(
     rotary_cos: torch.Tensor | None = None,
     rotary_sin: torch.Tensor | None = None,
     return_softmax_lse: bool = False,
+    *,
+    k_scale: float | None = None,
+    v_scale: float | None = None,
 ) -> torch.Tensor:
     """Paged or dense KV-cache attention with optional append (api.py:151-286).
 
     Appending ``k``/``v`` writes the caches and advances ``cache_seqlens`` in
     place on the device, like the reference.
+
+    Extension beyond the reference: ``k_cache``/``v_cache`` may be
+    ``torch.float8_e4m3fn`` (head dim 128, q in fp16/bf16); the attended
+    values are ``k_cache * k_scale`` and ``v_cache * v_scale`` (default 1.0).
+    Appended ``k``/``v`` must then already be e4m3 with the same scales.
     """
     validate_softmax_scale(softmax_scale)
     if rotary_cos is not None or rotary_sin is not None:
@@ -153,7 +162,12 @@ def flash_attn_with_kvcache(
         raise ValueError("q and cache tensors must have rank 4 and matching k/v cache shapes")
     if q.device != k_cache.device or q.device != v_cache.device:
         raise ValueError("q and cache tensors must be on the same device")
-    if q.dtype != k_cache.dtype or q.dtype != v_cache.dtype:
+    fp8_cache = k_cache.dtype == _FP8
+    if fp8_cache:
+        _validate_fp8_cache(q, k_cache, v_cache, k, v, k_scale, v_scale)
+    elif k_scale is not None or v_scale is not None:
+        raise ValueError("k_scale / v_scale apply to float8_e4m3fn caches only")
+    elif q.dtype != k_cache.dtype or q.dtype != v_cache.dtype:
         raise ValueError("q and cache tensors must have the same dtype")
     if q.dtype not in (torch.float16, torch.bfloat16, torch.float32):
         raise TypeError("supported dtypes are float16, bfloat16, and float32 for reference execution")
@@ -171,7 +185,8 @@ def flash_attn_with_kvcache(
         raise ValueError("appended k and v must have identical rank-4 shapes")
     if k is not None and (k.shape[0] != q.shape[0] or k.shape[2:] != k_cache.shape[2:]):
         raise ValueError("appended k/v must match batch, kv heads, and head dimension")
-    if k is not None and (k.device != q.device or k.dtype != q.dtype or v.device != q.device or v.dtype != q.dtype):
+    if k is not None and not fp8_cache and (k.device != q.device or k.dtype != q.dtype or v.device != q.device
+                                            or v.dtype != q.dtype):
         raise ValueError("appended k/v must match the query device and dtype")
     if cache_seqlens is None:
         raise ValueError("cache_seqlens is required for dense and paged caches")
@@ -196,9 +211,27 @@ def flash_attn_with_kvcache(
         raise ValueError("dense cache batch dimension must match q")
     if os.getenv("MXFLASHATTN_STRICT_VALIDATION", "0") == "1":
         _strict_kvcache_checks(k_cache, k, cache_seqlens, block_table)
-    return dispatch(
-        "flash_attn_with_kvcache",
-        q,
-        (q, k_cache, v_cache, k, v, cache_seqlens, block_table, _resolved_scale(q.shape[-1], softmax_scale),
-         causal),
-    )
+    args = (q, k_cache, v_cache, k, v, cache_seqlens, block_table, _resolved_scale(q.shape[-1], softmax_scale),
+            causal)
+    if fp8_cache:
+        args += (1.0 if k_scale is None else float(k_scale), 1.0 if v_scale is None else float(v_scale))
+    return dispatch("flash_attn_with_kvcache", q, args)
+
+
+_FP8 = getattr(torch, "float8_e4m3fn", None)
+
+
+def _validate_fp8_cache(q, k_cache, v_cache, k, v, k_scale, v_scale) -> None:
+    """Guards of the e4m3 cache extension (no reference counterpart)."""
+    if v_cache.dtype != k_cache.dtype:
+        raise ValueError("k_cache and v_cache must have the same dtype")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("float8_e4m3fn caches need a float16 or bfloat16 query")
+    if q.shape[3] != 128:
+        raise ValueError("float8_e4m3fn caches need head dimension 128")
+    for name, value in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if value is not None and not (math.isfinite(float(value)) and float(value) > 0.0):
+            raise ValueError(f"{name} must be a positive finite number")
+    if k is not None and (k.dtype != k_cache.dtype or v.dtype != k_cache.dtype or k.device != q.device
+                          or v.device != q.device):
+        raise ValueError("appended k/v for a float8_e4m3fn cache must be float8_e4m3fn on the query device")

@@ -135,7 +135,8 @@ def split_counters(device, stream_handle: int, nbytes: int):
 
 def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
                       append_len: int = 0, return_lse: bool = False, num_splits: int = 0, chunk_len: int = 0,
-                      out=None, k_new=None, v_new=None, single_launch: bool = True):
+                      out=None, k_new=None, v_new=None, single_launch: bool = True, k_scale: float = 1.0,
+                      v_scale: float = 1.0):
     """Attention of q [B, Sq, HQ, D] over the cached tokens (+ ``append_len``).
 
     ``cache_seqlens`` holds the lengths before the append.  Without
@@ -144,7 +145,8 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
     the caches first (``mxfa_kvcache_append_attention_launch``).
     ``num_splits``/``chunk_len`` 0 = library plan.  A split plan runs as one
     launch (the last split CTA of each unit merges) unless ``single_launch``
-    is False, which keeps the separate combine kernel.
+    is False, which keeps the separate combine kernel.  ``torch.float8_e4m3fn``
+    caches attend to ``k_cache * k_scale`` and ``v_cache * v_scale``.
     """
     B, Sq, HQ, D = q.shape
     q = _contig(q)
@@ -176,7 +178,16 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
         counters = None
         if num_splits > 1 and single_launch:
             counters = split_counters(q.device, stream, int(lib.mxfa_split_counter_bytes(B, Sq, HQ, HKV)))
-        if k_new is None:
+        if _is_fp8(k_cache):
+            if k_new is not None:
+                raise ValueError("the fused append does not take float8_e4m3fn rows; append with kv_append first")
+            name = "mxfa_kvcache_attention_fp8_launch"
+            rc = lib.mxfa_kvcache_attention_fp8_launch(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(),
+                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, _lib.ptr(counters), B, Sq, HQ, HKV, D, PS,
+                btw, pages, int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q),
+                float(softmax_scale), float(k_scale), float(v_scale), stream)
+        elif k_new is None:
             if counters is None:
                 name = "mxfa_kvcache_attention_launch"
                 rc = lib.mxfa_kvcache_attention_launch(
@@ -203,12 +214,16 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
     return (out, lse) if return_lse else out
 
 
+def _is_fp8(t) -> bool:
+    return t.dtype == getattr(torch, "float8_e4m3fn", None)
+
+
 def fused_append_supported(q, k_cache, k) -> bool:
     """True when one launch can append ``k``/``v`` and attend (up to 16 query rows per KV head)."""
     B, Sq, HQ, D = q.shape
     HKV = k_cache.shape[2]
     return (k is not None and k.shape[1] > 0 and HQ % HKV == 0 and Sq * (HQ // HKV) <= 16
-            and k.dtype == k_cache.dtype)
+            and k.dtype == k_cache.dtype and not _is_fp8(k_cache))
 
 
 def kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table) -> None:
@@ -239,7 +254,8 @@ def seqlens_add_(cache_seqlens: torch.Tensor, delta: int) -> None:
     _lib.check(rc, "mxfa_seqlens_add_launch")
 
 
-def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, softmax_scale, causal):
+def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, softmax_scale, causal,
+                            k_scale: float = 1.0, v_scale: float = 1.0):
     """``flash_attn_with_kvcache`` semantics of the reference (reference.py:88-139).
 
     Appends ``k``/``v`` (when given) at the current lengths, attends over the
@@ -263,7 +279,7 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_tabl
         kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
         append_len = k.shape[1]
     out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
-                            append_len=append_len)
+                            append_len=append_len, k_scale=k_scale, v_scale=v_scale)
     if k is not None:
         seqlens_add_(cache_seqlens, append_len)
     return out

@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -169,12 +170,12 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int D, int HKV, long long
 
 // ------------------------------------------------------------------ decode
 
-template <typename T, int HD, int NT, bool kTma>
+template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
 int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv,
                        cudaStream_t st) {
   static std::atomic<unsigned long long> done{0};
-  auto kern = paged_decode_kernel<T, HD, NT, kTma>;
-  const int smem = DecodeCfg<HD, NT>::kSmemBytes;
+  auto kern = paged_decode_kernel<T, HD, NT, kTma, kFp8>;
+  const int smem = DecodeCfg<HD, NT, kFp8>::kSmemBytes;
   if (int rc = ensure_smem(kern, smem, done)) return rc;
   kern<<<grid, kDecThreads, smem, st>>>(p, tk, tv);
   return check_launch("paged_decode_kernel");
@@ -190,8 +191,43 @@ int launch_decode_t(const DecodeParams& p, int nt, bool tma, dim3 grid, const CU
              : launch_decode_inst<T, HD, 2, false>(p, grid, tk, tv, st);
 }
 
-// Runs the decode kernel (split or direct) for a validated configuration.
-int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
+template <typename T>
+int launch_decode_fp8(const DecodeParams& p, int nt, bool tma, dim3 grid, const CUtensorMap& tk,
+                      const CUtensorMap& tv, cudaStream_t st) {
+  if (nt == 1)
+    return tma ? launch_decode_inst<T, 128, 1, true, true>(p, grid, tk, tv, st)
+               : launch_decode_inst<T, 128, 1, false, true>(p, grid, tk, tv, st);
+  return tma ? launch_decode_inst<T, 128, 2, true, true>(p, grid, tk, tv, st)
+             : launch_decode_inst<T, 128, 2, false, true>(p, grid, tk, tv, st);
+}
+
+// 4-D view over BOTH e4m3 caches (D = 128: one 128-byte row per head): dims
+// (128 bytes, head, slot row, K|V) with byte strides (128, HKV*128, distance
+// between the caches); the box (128, 1, 16, 2) is a whole K+V tile.
+bool encode_kv_map_fp8(CUtensorMap* map, const void* k, const void* v, int HKV, long long slots, int* swap) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const uintptr_t ka = reinterpret_cast<uintptr_t>(k), va = reinterpret_cast<uintptr_t>(v);
+  if (((ka | va) & 15) != 0 || ka == va) return false;
+  if (slots <= 0 || slots > 0xFFFFFFFFll) return false;
+  const uintptr_t lo = ka < va ? ka : va;
+  const unsigned long long dist = ka < va ? va - ka : ka - va;
+  if (dist >= (1ull << 40)) return false;
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(HKV), static_cast<cuuint64_t>(slots), 2};
+  cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(HKV) * 128, static_cast<cuuint64_t>(dist)};
+  cuuint32_t box[4] = {128, 1, static_cast<cuuint32_t>(kTileTok), 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, reinterpret_cast<void*>(lo), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  *swap = va < ka ? 1 : 0;
+  return true;
+}
+
+// Runs the decode kernel (split or direct) for a validated configuration;
+// kv_fp8: the caches hold e4m3 (D = 128 only).
+int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st, bool kv_fp8 = false) {
   const int rows_kv = p.Sq * p.GQ;
   const int nt = rows_kv <= 8 ? 1 : 2;
   const int row_groups = (rows_kv + 8 * nt - 1) / (8 * nt);
@@ -202,6 +238,14 @@ int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st) {
   std::memset(&tk, 0, sizeof(tk));
   std::memset(&tv, 0, sizeof(tv));
   bool tma = (p.PS % kTileTok) == 0;
+  if (kv_fp8) {
+    if (D != 128) return fail(MXFA_ERR_UNSUPPORTED, "FP8 caches need head dim 128 (got %d)", D);
+    int swap = 0;
+    if (tma) tma = encode_kv_map_fp8(&tk, p.k, p.v, p.HKV, static_cast<long long>(p.P) * p.PS, &swap);
+    p.kv_swap = tma ? swap : 0;
+    return bf16 ? launch_decode_fp8<__nv_bfloat16>(p, nt, tma, grid, tk, tv, st)
+                : launch_decode_fp8<__half>(p, nt, tma, grid, tk, tv, st);
+  }
   if (tma) {
     const long long slots = static_cast<long long>(p.P) * p.PS;
     // fewest copies per tile that the driver accepts: K+V in one box, else
@@ -330,7 +374,8 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
                                   void* workspace, size_t workspace_bytes, int B, int Sq, int HQ, int HKV, int D,
                                   int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
                                   int causal, int bf16, float scale, const void* k_new, const void* v_new,
-                                  unsigned* counters, void* stream) {
+                                  unsigned* counters, void* stream, bool kv_fp8 = false, float k_scale = 1.f,
+                                  float v_scale = 1.f) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
@@ -358,7 +403,8 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   p.GQ = HQ / HKV;
   p.append_len = append_len;
   p.causal = causal ? 1 : 0;
-  p.scale_log2 = scale * kLog2e;
+  p.scale_log2 = scale * kLog2e * (kv_fp8 ? k_scale : 1.f);
+  p.v_scale = kv_fp8 ? v_scale : 1.f;
   p.k_new = k_new;
   p.v_new = v_new;
   const int max_len = block_table ? BTW * PS : PS;
@@ -369,7 +415,7 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   if (num_splits <= 1) {
     p.NP = 1;
     p.c_len = max_len;
-    return run_decode(p, D, bf16 != 0, st);
+    return run_decode(p, D, bf16 != 0, st, kv_fp8);
   }
   const long long rows = static_cast<long long>(B) * Sq * HQ;
   const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
@@ -386,9 +432,9 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
     // one launch: the last split CTA of every unit merges the partials
     if (reinterpret_cast<uintptr_t>(counters) & 3) return fail(MXFA_ERR_INVALID, "counters must be 4-byte aligned");
     p.counters = counters;
-    return run_decode(p, D, bf16 != 0, st);
+    return run_decode(p, D, bf16 != 0, st, kv_fp8);
   }
-  if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
+  if (int rc = run_decode(p, D, bf16 != 0, st, kv_fp8)) return rc;
   return run_combine<false>(p.ows, p.mdws, out, nullptr, lse, static_cast<int>(rows), D, num_splits, bf16 != 0, st);
 }
 
@@ -420,6 +466,19 @@ int mxfa_kvcache_attention_launch(const void* q, const void* k_cache, const void
   return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
                                 Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
                                 scale, nullptr, nullptr, nullptr, stream);
+}
+
+int mxfa_kvcache_attention_fp8_launch(const void* q, const void* k_cache, const void* v_cache,
+                                      const int32_t* block_table, const int32_t* seqlens, void* out, float* lse,
+                                      void* workspace, size_t workspace_bytes, unsigned* counters, int B, int Sq,
+                                      int HQ, int HKV, int D, int PS, int BTW, int num_pages, int append_len,
+                                      int num_splits, int chunk_len, int causal, int bf16, float scale,
+                                      float k_scale, float v_scale, void* stream) {
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return fail(MXFA_ERR_INVALID, "k_scale / v_scale must be positive and finite");
+  return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
+                                Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
+                                scale, nullptr, nullptr, counters, stream, true, k_scale, v_scale);
 }
 
 int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_cache,

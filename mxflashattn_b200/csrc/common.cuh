@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -236,6 +237,26 @@ struct Elem<__half> {
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 };
+
+// Four e4m3 values (byte 0 first) -> two f16x2: lo = bytes (0, 1), hi =
+// bytes (2, 3).  Exact: every e4m3 value is an f16.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t quad, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(quad));
+}
+
+// A packed pair of T (bf16 or f16) as f16x2.
+template <typename T>
+__device__ __forceinline__ uint32_t to_f16x2(uint32_t v) {
+  if constexpr (std::is_same_v<T, __half>) {
+    return v;
+  } else {
+    const float2 f = Elem<T>::unpack(v);
+    return Elem<__half>::pack(f.x, f.y);
+  }
+}
 
 // Hardware base-2 exponential (MUFU); exp2(-inf) = +0.
 __device__ __forceinline__ float fast_exp2(float x) {

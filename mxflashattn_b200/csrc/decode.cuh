@@ -23,6 +23,8 @@
 // 563-577, 846-853, 862-888); the attention math of mxflashattn/reference.py.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace mxfa {
@@ -53,6 +55,9 @@ struct DecodeParams {
   // split CTAs of a unit merges the unit's partials into out / lse and
   // resets its counter to zero.
   unsigned* counters;
+  // FP8 (e4m3) caches: dequantised value = stored * scale.  k_scale is folded
+  // into scale_log2 by the launcher; v_scale multiplies the output.
+  float v_scale;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -72,16 +77,21 @@ constexpr int kTileTok = 16;
 //   HD=128, 16 query rows: 2 CTAs x 12 slots (96 KB)
 //   HD=64,  8 query rows : 4 CTAs x 12 slots (48 KB, <=102 regs)
 //   HD=64,  16 query rows: 3 CTAs x 16 slots (64 KB)
-template <int HD, int NT>
+template <int HD, int NT, bool kFp8 = false>
 struct DecodeCfg {
-  static constexpr int kCtasPerSm = HD == 128 ? (NT == 1 ? 3 : 2) : (NT == 1 ? 4 : 3);
-  static constexpr int kDBlk = HD / 64;                  // 128-byte column blocks per row
+  static constexpr int kCtasPerSm =
+      kFp8 ? (NT == 1 ? 4 : 2) : (HD == 128 ? (NT == 1 ? 3 : 2) : (NT == 1 ? 4 : 3));
+  static constexpr int kElemBytes = kFp8 ? 1 : 2;
+  static constexpr int kRowBytes = HD * kElemBytes;      // one cached row of one head
+  static constexpr int kRowChunks = kRowBytes / 16;      // 16-byte chunks per row
+  static constexpr int kDBlk = kRowBytes / 128;          // 128-byte column blocks per row
   static constexpr int kBlkBytes = kTileTok * 128;       // one column block of one tile: 2 KB
-  static constexpr int kTileBytes = kTileTok * HD * 2;   // K (or V) bytes of one tile
+  static constexpr int kTileBytes = kTileTok * kRowBytes;  // K (or V) bytes of one tile
   static constexpr int kSlotBytes = 2 * kTileBytes;      // K + V
   static constexpr int kSlots = (192 * 1024 / kCtasPerSm) / kSlotBytes / 4 * 4;  // multiple of the consumer count
   static constexpr int kRingBytes = kSlots * kSlotBytes;
   static constexpr int kSmemBytes = kRingBytes + 2 * kSlots * 8 + 1024;
+  static_assert(kDBlk >= 1, "rows narrower than one 128-byte swizzle block are not supported");
 };
 
 // Merge scratch laid over the ring once all tiles are consumed.
@@ -184,11 +194,14 @@ __device__ __forceinline__ void merge_split_row(const float* ows, const float* m
   if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
 }
 
-template <typename T, int HD, int NT, bool kTma>
-__global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
+// kFp8: e4m3 caches.  Tiles are dequantised in registers (cvt e4m3x2 ->
+// f16x2, exact) and both products run in f16; q is converted to f16 once.
+template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
+__global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPerSm)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
-  using Cfg = DecodeCfg<HD, NT>;
+  using Cfg = DecodeCfg<HD, NT, kFp8>;
+  using MT = std::conditional_t<kFp8, __half, T>;  // tensor-core operand type
   static_assert(DecodeMerge<HD, NT>::kBytes <= Cfg::kRingBytes, "merge scratch must fit the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     const int capacity = p.bt != nullptr ? p.BTW * p.PS : p.PS;
     if (threadIdx.x == 0 && z == 0 && rg == 0 && total_len > capacity)
       raise_flag(p.bt != nullptr ? MXFA_FLAG_TABLE_TOO_NARROW : MXFA_FLAG_DENSE_OVERFLOW);
-    constexpr int kChunks = HD / 8;
+    constexpr int kChunks = Cfg::kRowChunks;
     for (int c = threadIdx.x; c < (a_hi - a_lo) * kChunks; c += blockDim.x) {
       const int pos = a_lo + c / kChunks;
       const int ch = c % kChunks;
@@ -295,12 +308,13 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
         raise_flag(MXFA_FLAG_PAGE_OUT_OF_RANGE);
         continue;
       }
-      const size_t src = ((static_cast<size_t>(b) * p.append_len + (pos - old_len)) * p.HKV + kvh) * HD + ch * 8;
-      const size_t dst = ((static_cast<size_t>(phys) * p.PS + pos % p.PS) * p.HKV + kvh) * HD + ch * 8;
-      *reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + dst) =
-          *reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_new) + src);
-      *reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + dst) =
-          *reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_new) + src);
+      const size_t src =
+          ((static_cast<size_t>(b) * p.append_len + (pos - old_len)) * p.HKV + kvh) * Cfg::kRowBytes + ch * 16;
+      const size_t dst = ((static_cast<size_t>(phys) * p.PS + pos % p.PS) * p.HKV + kvh) * Cfg::kRowBytes + ch * 16;
+      *reinterpret_cast<uint4*>(const_cast<uint8_t*>(static_cast<const uint8_t*>(p.k)) + dst) =
+          *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.k_new) + src);
+      *reinterpret_cast<uint4*>(const_cast<uint8_t*>(static_cast<const uint8_t*>(p.v)) + dst) =
+          *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.v_new) + src);
     }
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
@@ -316,8 +330,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
 
   // ---------------------------------------------------------------- producer
   if (warp == kDecConsumerWarps) {
-    const T* kc = static_cast<const T*>(p.k);
-    const T* vc = static_cast<const T*>(p.v);
+    const uint8_t* kc = static_cast<const uint8_t*>(p.k);
+    const uint8_t* vc = static_cast<const uint8_t*>(p.v);
     if constexpr (kTma) {
       if (lane == 0) {
         prefetch_tensormap(&tmk);
@@ -343,7 +357,10 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
               mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kTileBytes);
               uint8_t* kd = ring + slot * Cfg::kSlotBytes;
               uint8_t* vd = kd + Cfg::kTileBytes;
-              if (p.kv_map == 5) {
+              if constexpr (kFp8) {
+                // one box: (128 bytes = one row, head, 16 rows, K|V)
+                tma_load_4d(ring + slot * Cfg::kSlotBytes, &tmk, &full[slot], 0, kvh, row, 0);
+              } else if (p.kv_map == 5) {
                 // one box: (64 columns, head, 16 rows, column block, K|V)
                 tma_load_5d(ring + slot * Cfg::kSlotBytes, &tmk, &full[slot], 0, kvh, row, 0, 0);
               } else if (p.kv_map == 4) {
@@ -369,7 +386,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
         for (int tt = max(issued - Cfg::kSlots, 0); tt < issued; ++tt)
           mbar_wait(&full[tt % Cfg::kSlots], (tt / Cfg::kSlots) & 1);
     } else {
-      constexpr int kRowChunks = HD / 8;               // 16-byte chunks per row
+      constexpr int kRowChunks = Cfg::kRowChunks;
       constexpr int kChunks = kTileTok * kRowChunks;  // per tile per tensor (a multiple of 32)
       for (int t = 0; t < ntiles; ++t) {
         const int slot = t % Cfg::kSlots;
@@ -401,7 +418,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
               mapped = false;
             }
             if (mapped)
-              roff = ((static_cast<long long>(phys) * p.PS + (pos % p.PS)) * p.HKV + kvh) * HD;
+              roff = ((static_cast<long long>(phys) * p.PS + (pos % p.PS)) * p.HKV + kvh) * Cfg::kRowBytes;
           }
         }
 #pragma unroll 4
@@ -411,8 +428,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
           const long long off = __shfl_sync(0xffffffffu, roff, r);
           if (off < 0) continue;
           const uint32_t so = (ch >> 3) * Cfg::kBlkBytes + swz128(r, ch & 7);
-          cp_async_16(kd + so, kc + off + ch * 8);
-          cp_async_16(vd + so, vc + off + ch * 8);
+          cp_async_16(kd + so, kc + off + ch * 16);
+          cp_async_16(vd + so, vc + off + ch * 16);
         }
         cp_async_mbar_arrive_noinc(&full[slot]);
       }
@@ -442,8 +459,18 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     }
 #pragma unroll
     for (int kk = 0; kk < HD / 16; ++kk) {
-      qf[kk][nt][0] = qr ? ld_u32(qr + kk * 16 + 2 * t4) : 0u;
-      qf[kk][nt][1] = qr ? ld_u32(qr + kk * 16 + 8 + 2 * t4) : 0u;
+      if constexpr (kFp8) {
+        // fp8 K fragments come out of ldmatrix with D permuted inside each
+        // 16-column step (thread t4 holds columns 4*t4 .. 4*t4+3); q is loaded
+        // in the same order and converted to f16
+        uint2 v = make_uint2(0u, 0u);
+        if (qr) v = *reinterpret_cast<const uint2*>(qr + kk * 16 + 4 * t4);
+        qf[kk][nt][0] = to_f16x2<T>(v.x);
+        qf[kk][nt][1] = to_f16x2<T>(v.y);
+      } else {
+        qf[kk][nt][0] = qr ? ld_u32(qr + kk * 16 + 2 * t4) : 0u;
+        qf[kk][nt][1] = qr ? ld_u32(qr + kk * 16 + 8 + 2 * t4) : 0u;
+      }
     }
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -478,9 +505,9 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     const bool partial = (pos0 < lo) || (pos0 + kTileTok > hi);
     if (partial) {
       // rows outside [lo, hi) may hold padding (even NaN): zero their V so p=0 rows add nothing
-      for (int c = lane; c < kTileTok * (HD / 8); c += 32) {
-        const int r = c / (HD / 8);
-        const int ch = c % (HD / 8);
+      for (int c = lane; c < kTileTok * Cfg::kRowChunks; c += 32) {
+        const int r = c / Cfg::kRowChunks;
+        const int ch = c % Cfg::kRowChunks;
         const int pos = pos0 + r;
         if (pos < lo || pos >= hi)
           *reinterpret_cast<uint4*>(vd + (ch >> 3) * Cfg::kBlkBytes + swz128(r, ch & 7)) =
@@ -494,7 +521,26 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
     float s[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-    {
+    if constexpr (kFp8) {
+      // one ldmatrix.x4 = two 16-column steps x two 8-token halves of fp8 K;
+      // each register (4 e4m3 values) becomes the step's low and high f16x2
+      const int q8 = lane >> 3;
+      const int r = ((q8 & 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int c2 = 0; c2 < HD / 32; ++c2) {
+        uint32_t x[4];
+        ldsm_x4(kbase + swz128(r, 2 * c2 + (q8 >> 1)), x[0], x[1], x[2], x[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int kk = 2 * c2 + h;
+          uint32_t lo0, hi0, lo1, hi1;
+          e4m3x4_to_f16x2x2(x[2 * h], lo0, hi0);
+          e4m3x4_to_f16x2x2(x[2 * h + 1], lo1, hi1);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Elem<MT>::mma(s[nt], lo0, lo1, hi0, hi1, qf[kk][nt][0], qf[kk][nt][1]);
+        }
+      }
+    } else {
       const int q8 = lane >> 3;
       const int r = ((q8 & 1) << 3) + (lane & 7);
 #pragma unroll
@@ -503,7 +549,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
         uint32_t a0, a1, a2, a3;
         ldsm_x4(kbase + (dch >> 3) * Cfg::kBlkBytes + swz128(r, dch & 7), a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Elem<T>::mma(s[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
+        for (int nt = 0; nt < NT; ++nt) Elem<MT>::mma(s[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
       }
     }
 
@@ -566,12 +612,41 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const float a = s[nt][2 * hh], c = s[nt][2 * hh + 1];
-        const uint32_t hi = Elem<T>::pack(a, c);
-        const float2 hf = Elem<T>::unpack(hi);
+        const uint32_t hi = Elem<MT>::pack(a, c);
+        const float2 hf = Elem<MT>::unpack(hi);
         pb[nt][hh] = movmatrix_trans(hi);
-        pl[nt][hh] = movmatrix_trans(Elem<T>::pack(a - hf.x, c - hf.y));
+        pl[nt][hh] = movmatrix_trans(Elem<MT>::pack(a - hf.x, c - hf.y));
       }
-    {
+    if constexpr (kFp8) {
+      // fp8 V rows are loaded untransposed (same addressing as K), widened to
+      // f16 and transposed in registers: the low and high f16x2 of a register
+      // give O^T rows {4j, 4j+1} and {4j+2, 4j+3} of the 16-column step, so
+      // accumulator row g of step mi holds D column 16*mi + 4*(g/2) + g%2 and
+      // row g+8 holds that column + 2 (undone when the warps merge)
+      const int q8 = lane >> 3;
+      const int r = ((q8 & 1) << 3) + (lane & 7);
+#pragma unroll
+      for (int c2 = 0; c2 < HD / 32; ++c2) {
+        uint32_t y[4];
+        ldsm_x4(vbase + swz128(r, 2 * c2 + (q8 >> 1)), y[0], y[1], y[2], y[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int mi = 2 * c2 + h;
+          uint32_t l0, h0, l1, h1;
+          e4m3x4_to_f16x2x2(y[2 * h], l0, h0);
+          e4m3x4_to_f16x2x2(y[2 * h + 1], l1, h1);
+          const uint32_t a0 = movmatrix_trans(l0);
+          const uint32_t a1 = movmatrix_trans(h0);
+          const uint32_t a2 = movmatrix_trans(l1);
+          const uint32_t a3 = movmatrix_trans(h1);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+            Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+          }
+        }
+      }
+    } else {
       const int q8 = lane >> 3;
       const int r = ((q8 >> 1) << 3) + (lane & 7);
 #pragma unroll
@@ -581,8 +656,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
         ldsm_x4_trans(vbase + (dch >> 3) * Cfg::kBlkBytes + swz128(r, dch & 7), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-          Elem<T>::mma(o[mi][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+          Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
         }
       }
     }
@@ -614,8 +689,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT>::kCtasPerSm)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int col = nt * 8 + 2 * t4 + (e & 1);
-        const int d = mi * 16 + g + ((e >> 1) << 3);
-        om[(warp * Mg::kCols + col) * Mg::kStride + d] = o[mi][nt][e];
+        const int d = kFp8 ? mi * 16 + 4 * (g >> 1) + (g & 1) + ((e >> 1) << 1) : mi * 16 + g + ((e >> 1) << 3);
+        om[(warp * Mg::kCols + col) * Mg::kStride + d] = kFp8 ? o[mi][nt][e] * p.v_scale : o[mi][nt][e];
       }
   if (g == 0) {
 #pragma unroll

@@ -188,3 +188,54 @@ def test_availability_check_failure_is_reported(monkeypatch):
     monkeypatch.setattr(dispatch, "_native_extension", lambda: SimpleNamespace(is_available=broken))
     assert dispatch.native_unavailable_reason(_cuda_like(), "flash_attn_func").startswith(
         "native_availability_check_failed:OSError")
+
+
+# ------------------------------------------------ FP8 (e4m3) cache extension
+
+def _fp8_paged(head_dim=128, q_dtype=torch.bfloat16):
+    q = torch.randn(2, 1, 4, head_dim).to(q_dtype)
+    kc = torch.randn(6, 16, 2, head_dim).to(torch.float8_e4m3fn)
+    vc = torch.randn(6, 16, 2, head_dim).to(torch.float8_e4m3fn)
+    return q, kc, vc, torch.tensor([3, 5], dtype=torch.int32), torch.zeros((2, 3), dtype=torch.int32)
+
+
+@pytest.mark.parametrize("kwargs,match", [
+    (dict(k_scale=0.0), "k_scale must be a positive finite number"),
+    (dict(v_scale=float("nan")), "v_scale must be a positive finite number"),
+])
+def test_fp8_cache_rejects_bad_scales(kwargs, match):
+    q, kc, vc, sl, bt = _fp8_paged()
+    with pytest.raises(ValueError, match=match):
+        flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt, **kwargs)
+
+
+def test_fp8_cache_guards():
+    q, kc, vc, sl, bt = _fp8_paged(head_dim=64)
+    with pytest.raises(ValueError, match="head dimension 128"):
+        flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt)
+    q, kc, vc, sl, bt = _fp8_paged(q_dtype=torch.float32)
+    with pytest.raises(TypeError, match="float16 or bfloat16 query"):
+        flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt)
+    q, kc, vc, sl, bt = _fp8_paged()
+    with pytest.raises(ValueError, match="same dtype"):
+        flash_attn_with_kvcache(q, kc, vc.to(torch.bfloat16), cache_seqlens=sl, block_table=bt)
+    k_new = torch.randn(2, 1, 2, 128).to(torch.bfloat16)
+    with pytest.raises(ValueError, match="must be float8_e4m3fn"):
+        flash_attn_with_kvcache(q, kc, vc, k=k_new, v=k_new, cache_seqlens=sl, block_table=bt)
+
+
+def test_scales_are_rejected_for_16_bit_caches():
+    q, k, v = tensors(head_dim=128)
+    with pytest.raises(ValueError, match="float8_e4m3fn caches only"):
+        flash_attn_with_kvcache(q, k, v, cache_seqlens=torch.tensor([3], dtype=torch.int32), k_scale=0.5)
+
+
+def test_fp8_scales_reach_the_backend(monkeypatch):
+    calls = []
+    ext = SimpleNamespace(is_available=lambda: True,
+                          flash_attn_with_kvcache=lambda *args: calls.append(args) or "result")
+    monkeypatch.setattr(dispatch, "_native_extension", lambda: ext)
+    monkeypatch.setattr(dispatch, "native_unavailable_reason", lambda tensor, op: None)
+    q, kc, vc, sl, bt = _fp8_paged()
+    assert flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt, k_scale=0.5, v_scale=2.0) == "result"
+    assert calls[0][-2:] == (0.5, 2.0)
