@@ -35,6 +35,7 @@ from mxflashattn_b200.integrations.vllm.decoder_adapter import DecoderAdapterBlo
 
 _worker_event_count = 0
 _plugin_log = os.getenv("MXFLASHATTN_PLUGIN_IMPORT_LOG")
+_shadow_calls = 0
 
 
 def _record_worker_event(event: dict) -> None:
@@ -248,12 +249,47 @@ class MXFlashAttnImpl(FlashAttentionImpl):
         _record_worker_event(event)
         if output is None:
             raise ValueError("vLLM must provide an output buffer")
+        _shadow_check(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale,
+                      output_block_scale, result)
         target = output[: result.shape[0]]
         if target.numel() != result.numel():
             raise RuntimeError(f"MXFlashAttn decoder output size mismatch: target={tuple(target.shape)} "
                                f"result={tuple(result.shape)}")
         target.copy_(result.reshape_as(target))
         return output
+
+
+def _shadow_check(impl, layer, query, key, value, kv_cache, attn_metadata, output, output_scale,
+                  output_block_scale, result) -> None:
+    """Every MXFLASHATTN_SHADOW_CHECK_EVERY-th decode call, also run vLLM's own
+    attention on the same live inputs and record the largest difference.
+
+    A debug aid for end-to-end parity (no reference counterpart): it syncs the
+    device and doubles the checked call's attention cost, so it is off unless
+    the variable is set.  Re-running vLLM's forward re-writes the same cache
+    rows, which leaves the cache unchanged.
+    """
+    global _shadow_calls
+    every = int(os.getenv("MXFLASHATTN_SHADOW_CHECK_EVERY", "0") or 0)
+    if every <= 0:
+        return
+    _shadow_calls += 1
+    if _shadow_calls % every != 1 and every != 1:
+        return
+    import torch
+
+    ref = torch.zeros_like(output)
+    FlashAttentionImpl.forward(impl, layer, query, key, value, kv_cache, attn_metadata, ref, output_scale,
+                               output_block_scale)
+    n = result.shape[0]
+    mine = result.reshape(n, -1).float()
+    theirs = ref[:n].reshape(n, -1).float()
+    _record_worker_event({
+        "path": "shadow_check",
+        "tokens": int(n),
+        "max_abs_diff": float((mine - theirs).abs().max()),
+        "max_abs_ref": float(theirs.abs().max()),
+    })
 
 
 class MXFlashAttnBackend(FlashAttentionBackend):

@@ -193,3 +193,38 @@ def test_registration_points_flash_attn_at_the_plugin(plugin, monkeypatch):
     assert info["registered"] == "true"
     assert recorded["path"] == "mxflashattn_b200.integrations.vllm.vllm_plugin.MXFlashAttnBackend"
     assert plugin.MXFlashAttnBackend.get_impl_cls() is plugin.MXFlashAttnImpl
+
+
+# ------------------------------------------------ end-to-end script helpers
+
+def test_smoke_generate_model_dir_and_prompts(tmp_path):
+    import json as _json
+
+    from mxflashattn_b200.integrations.vllm import smoke_generate as sg
+
+    path = sg.write_model_dir("qwen3-4b", tmp_path)
+    cfg = _json.loads((path / "config.json").read_text())
+    assert cfg["num_attention_heads"] == 32 and cfg["num_key_value_heads"] == 8 and cfg["head_dim"] == 128
+    assert cfg["num_hidden_layers"] == 36 and cfg["architectures"] == ["Qwen3ForCausalLM"]
+    with pytest.raises(ValueError, match="unknown architecture"):
+        sg.write_model_dir("qwen3-1b", tmp_path)
+    a = sg.make_prompts(5, 10, 20, seed=3)
+    assert a == sg.make_prompts(5, 10, 20, seed=3)
+    assert all(10 <= len(p) <= 20 for p in a) and len(a) == 5
+
+
+def test_smoke_generate_compare_and_event_counts(tmp_path):
+    from mxflashattn_b200.integrations.vllm import smoke_generate as sg
+
+    base = {"outputs": [{"token_ids": [1, 2, 3, 4], "logprobs": [-1.0, -2.0, -3.0, -4.0]},
+                        {"token_ids": [5, 6], "logprobs": [-0.5, -0.25]}], "decode_tok_per_s": 10.0}
+    cand = {"outputs": [{"token_ids": [1, 2, 9, 4], "logprobs": [-1.0, -2.001, -3.5, -4.0]},
+                        {"token_ids": [5, 6], "logprobs": [-0.5, -0.25]}], "decode_tok_per_s": 12.0}
+    summary = sg.compare_runs(base, cand)
+    assert summary["token_agreement"] == 5 / 6
+    assert summary["first_divergence_min"] == 2
+    assert abs(summary["max_logprob_gap_before_divergence"] - 0.001) < 1e-9
+    log = tmp_path / "events.jsonl"
+    log.write_text('{"path": "cuda_sm100"}\n{"path": "cuda_sm100"}\n{"path": "vendor_prefill_or_blocked"}\n')
+    assert sg.count_events(log) == {"cuda_sm100": 2, "vendor_prefill_or_blocked": 1}
+    assert sg.count_events(tmp_path / "missing.jsonl") == {}
