@@ -1,23 +1,26 @@
 // prefill_sm100.cuh -- attention forward on the 5th-generation tensor cores
 // (tcgen05 MMA, accumulators in tensor memory, operands staged by TMA).
 //
-// CTA = one 128-row query tile of one head; 8 warps, specialised:
-//   warp 0   : TMA producer -- Q once, then K and V tiles (128 keys) into a
-//              two-stage ring, each stage guarded by full/empty mbarriers
-//   warp 1   : allocates tensor memory and issues every tcgen05.mma from one
-//              thread:  S_j = Q K_j^T  (M=128, N=128, K=D; both K-major)
-//                       O  += P_j V_j  (M=128, N=D,  K=128; V MN-major)
-//              committing each group to an mbarrier
-//   warps 4-7: softmax, one thread per query row (tensor-memory lane = row):
-//              read S_j with tcgen05.ld, mask, keep an online max in the log2
-//              domain, write P_j (bf16/fp16) into tensor memory for the P.V
-//              product (A operand read from TMEM), rescale O in tensor memory
-//              only when a row max grows by more than 2^8 (rare after the
-//              first tiles), and finally normalise O and store it.
-// Tensor memory: S double buffer (2 x 128 fp32 columns) | O (D columns) |
-// P double buffer (2 x 64 columns, two 16-bit values per column).
-// S_{j+1} is issued before P_j is ready, so the tensor pipe computes the next
-// scores while the softmax warps work on the current ones.
+// CTA = one 128-row query tile of one head; 12 warps, specialised:
+//   warp 0    : TMA producer -- Q once, then K and V tiles (128 keys) into a
+//               three-stage ring, each stage guarded by full/empty mbarriers
+//   warp 1    : allocates tensor memory and issues every tcgen05.mma from one
+//               thread:  S_j = Q K_j^T   (M=128, N=128, K=D; both K-major)
+//                        O_{j%2} += P_j V_j (M=128, N=D, K=128; P from tensor
+//                        memory, V MN-major), committing each to an mbarrier
+//   warps 4-7 : softmax group 0 -- key tiles 0, 2, 4, ...
+//   warps 8-11: softmax group 1 -- key tiles 1, 3, 5, ...
+// Each softmax group keeps its own online state (m, l) and its own output
+// accumulator O_g in tensor memory, like two interleaved splits of the key
+// range; the groups merge (m, l, O) once at the end.  Two groups put two
+// softmax warps on every SM sub-partition, so one warp's exp2 / conversion
+// latency overlaps the other's work, and the tensor pipe always has the other
+// group's products queued.  Per tile a group makes two passes over S in
+// tensor memory (row max, then exp2 + sum + bf16/fp16 pack), writing P_j over
+// the columns of S_j it has already read.
+// Tensor memory: S/P buffer 0 | S/P buffer 1 | O_0 | O_1 (128 + 128 + 2*D columns).
+// The next score product into a buffer is issued after the P.V product that
+// reads it; tcgen05.mma from one thread execute in issue order.
 //
 // Semantics follow mxflashattn/reference.py:8-85: GQA head h reads KV head
 // h / (HQ/HKV); causal masking is bottom-right aligned; a row that sees no
@@ -111,12 +114,43 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+#define MXFA_R64(x)                                                                                             \
+  MXFA_R32(x), "=r"(x[32]), "=r"(x[33]), "=r"(x[34]), "=r"(x[35]), "=r"(x[36]), "=r"(x[37]), "=r"(x[38]),       \
+      "=r"(x[39]), "=r"(x[40]), "=r"(x[41]), "=r"(x[42]), "=r"(x[43]), "=r"(x[44]), "=r"(x[45]), "=r"(x[46]),   \
+      "=r"(x[47]), "=r"(x[48]), "=r"(x[49]), "=r"(x[50]), "=r"(x[51]), "=r"(x[52]), "=r"(x[53]), "=r"(x[54]),   \
+      "=r"(x[55]), "=r"(x[56]), "=r"(x[57]), "=r"(x[58]), "=r"(x[59]), "=r"(x[60]), "=r"(x[61]), "=r"(x[62]),   \
+      "=r"(x[63])
+
+// 64 consecutive columns in one load (one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,"
+      "%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : MXFA_R64(r)
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
       "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
       "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
       MXFA_W32(r)
+      : "memory");
+}
+
+#define MXFA_W16(x)                                                                                             \
+  "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7]), "r"(x[8]), "r"(x[9]), \
+      "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]), "r"(x[15])
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      MXFA_W16(r)
       : "memory");
 }
 
@@ -141,8 +175,8 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool b_mn_major)
 
 constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
 constexpr int kTcKeys = 128;   // keys per tile (MMA N of S, K of P.V)
-constexpr int kTcThreads = 256;
-constexpr int kTcSoftmaxWarps = 4;
+constexpr int kTcThreads = 384;
+constexpr int kTcGroupWarps = 4;  // warps per softmax group (one per tensor-memory lane quadrant)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when a row max grows by > 2^8
 
 template <int HD>
@@ -154,19 +188,72 @@ struct TcCfg {
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kTile;
   static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kMl = kQ;                       // merge scratch over Q once every product is done
   static constexpr int kBar = kV + kStages * kTile;
-  static constexpr int kNumBars = 1 + 4 * kStages + 8;
+  static constexpr int kNumBars = 1 + 4 * kStages + 6;
   static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O | P0 P1
-  static constexpr uint32_t kTmemO = 256;
-  static constexpr uint32_t kTmemP = 384;               // two 64-column P buffers (128 keys, 2 per column)
+  static constexpr uint32_t kTmemCols = 512;           // S/P 0 | S/P 1 | O_0 | O_1
+  static constexpr uint32_t kTmemO = 2 * kTcKeys;      // O_g at kTmemO + g * HD
 };
 
 template <int kStages>
 struct TcBars {
   uint64_t q_full, k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], s_empty[2], p_full[2], pv_done[2];
+  uint64_t s_full[2], p_full[2], pv_done[2];
 };
+
+// ------------------------------------------------- softmax arithmetic off XU
+//
+// The softmax warps are bound by the XU pipe (MUFU ex2 and the f32 -> bf16x2
+// conversion both run there, at a fraction of the FMA/ALU rate).  Two
+// substitutions move work to the other pipes without changing the math:
+//
+// exp2_fma: 2^x on the FMA pipe for a share of the elements.  x is split into
+//   n = round(x) (a 1.5*2^23 add leaves n in the low mantissa bits) and
+//   f = x - n in [-0.5, 0.5]; 2^f is a degree-4 polynomial (coefficients from
+//   a relative-error least-squares fit on [-0.5, 0.5], max error 2.7e-6 in
+//   float), and 2^n is added to the exponent field with one integer add.
+//   x <= -126 (including -inf for masked keys) gives exactly 0.
+// pack_bf16_rne: two non-negative finite floats to bf16x2 with round to
+//   nearest even done by integer adds (bit-identical to cvt.rn.bf16x2.f32).
+#ifndef MXFA_PF_POLY_MASK
+#define MXFA_PF_POLY_MASK 0x88  // element e of a row uses exp2_fma when bit (e & 7) is set
+#endif
+
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float t = xc + 12582912.f;  // 1.5 * 2^23
+  const float n = t - 12582912.f;
+  const float f = xc - n;
+  float q = 0.009570610709488392f;
+  q = fmaf(q, f, 0.055917903780937195f);
+  q = fmaf(q, f, 0.24024732410907745f);
+  q = fmaf(q, f, 0.6931217908859253f);
+  q = fmaf(q, f, 0.9999992847442627f);
+  const float r = __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+  return x > -126.f ? r : 0.f;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16_rne(float a, float b) {
+  uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  ua += 0x7FFFu + ((ua >> 16) & 1u);
+  ub += 0x7FFFu + ((ub >> 16) & 1u);
+  return __byte_perm(ua, ub, 0x7632);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>)
+    return pack_bf16_rne(a, b);
+  else
+    return Elem<T>::pack(a, b);
+}
+
+// Element e of a row: 2^x on MUFU or on the FMA pipe (the choice folds to a
+// constant once the row loop is unrolled).
+__device__ __forceinline__ float softmax_exp2(float x, int e) {
+  return ((MXFA_PF_POLY_MASK >> (e & 7)) & 1) ? exp2_fma(x) : fast_exp2(x);
+}
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -193,6 +280,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   TcBars<NS>* bars = reinterpret_cast<TcBars<NS>*>(sm + Cfg::kBar);
+  float* ml = reinterpret_cast<float*>(sm + Cfg::kMl);  // [group][m | l][row]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kBar + Cfg::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -222,7 +310,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   T* outp = static_cast<T*>(p.out);
   if (nkt == 0) {  // every row of this tile sees no key: output 0, LSE -inf
-    if (warp >= 4) {
+    if (warp >= 4 && warp < 8) {
       const int r = (warp - 4) * 32 + lane;
       if (q0 + r < q_len) {
         T* orow = outp + (static_cast<size_t>(q_start + q0 + r) * p.HQ + h) * HD;
@@ -243,8 +331,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_empty[i], kTcSoftmaxWarps);
-      mbar_init(&bars->p_full[i], kTcSoftmaxWarps);
+      mbar_init(&bars->p_full[i], kTcGroupWarps);
       mbar_init(&bars->pv_done[i], 1);
     }
     *abort = 0;
@@ -293,7 +380,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t q_base = smem_u32(sm + Cfg::kQ);
       auto issue_s = [&](int t) -> bool {
         const int sb = t & 1, st = t % NS;
-        if (t >= 2 && !tc_wait(&bars->s_empty[sb], ((t >> 1) - 1) & 1, abort)) return false;
         if (!tc_wait(&bars->k_full[st], (t / NS) & 1, abort)) return false;
         tc_fence_after();
         const uint32_t k_base = smem_u32(sm + Cfg::kK + st * Cfg::kTile);
@@ -309,8 +395,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       bool ok = tc_wait(&bars->q_full, 0, abort);
       if (ok) ok = issue_s(0);
+      if (ok && nkt > 1) ok = issue_s(1);
       for (int j = 0; j < nkt && ok; ++j) {
-        if (j + 1 < nkt && !issue_s(j + 1)) break;
         const int pb = j & 1, vs = j % NS;
         if (!tc_wait(&bars->p_full[pb], (j >> 1) & 1, abort)) break;
         if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
@@ -319,60 +405,67 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk) {
           const uint64_t vd = smem_desc(v_base + kk * 16 * 128, Cfg::kBlk, 1024);
-          // 16 keys = 8 packed columns of the P buffer in tensor memory
-          umma_f16_ts(tmem + Cfg::kTmemO, tmem + Cfg::kTmemP + pb * 64 + kk * 8, vd, idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          // 16 keys = 8 packed columns of P_j (written over S_j in buffer j%2)
+          umma_f16_ts(tmem + Cfg::kTmemO + pb * HD, tmem + pb * kTcKeys + kk * 8, vd, idesc_o,
+                      (j >= 2 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done[pb]);
         umma_commit(&bars->v_empty[vs]);
+        // S_{j+2} reuses buffer j%2; it is issued after the P.V product above
+        if (j + 2 < nkt && !issue_s(j + 2)) break;
       }
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
-    const int r = (warp - 4) * 32 + lane;  // query row within the tile == tensor-memory lane
-    const int qi = q0 + r;                 // query index within the sequence
-    const uint32_t lane_base = tmem + ((static_cast<uint32_t>(warp - 4) * 32u) << 16);
+    const int g = (warp - 4) >> 2;          // group: key tiles j with j % 2 == g
+    const int quad = warp & 3;              // tensor-memory lane quadrant
+    const int r = quad * 32 + lane;         // query row within the tile == tensor-memory lane
+    const int qi = q0 + r;                  // query index within the sequence
+    const uint32_t lane_base = tmem + ((static_cast<uint32_t>(quad) * 32u) << 16);
+    const uint32_t o_base = lane_base + Cfg::kTmemO + g * HD;
     const int vis_end = p.causal ? min(k_len, qi + shift + 1) : k_len;  // keys [0, vis_end) visible
+    const float sc = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkt; ++j) {
-      const int sb = j & 1;
+    for (int j = g; j < nkt; j += 2) {
       // wait results are made warp-uniform: tcgen05.ld/st are warp-collective
-      if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[sb], (j >> 1) & 1, abort))) {
+      if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[g], (j >> 1) & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kTcKeys];
-#pragma unroll
-      for (int c = 0; c < kTcKeys; c += 32) {
-        uint32_t raw[32];
-        tmem_ld32(lane_base + sb * kTcKeys + c, raw);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(raw[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_empty[sb]);
-
-      // scores into the log2 domain; masked keys become -inf (after scaling, so
-      // a zero scale still gives -inf there and 0 elsewhere)
+      const uint32_t sbuf = lane_base + g * kTcKeys;
       const int key0 = j * kTcKeys;
-      float mx = -INFINITY;
-      if (key0 + kTcKeys <= vis_end) {
+      const bool full = key0 + kTcKeys <= vis_end;
+
+      // pass 1: the row's extreme raw score over visible keys (max for a
+      // positive scale, min for a negative one), scaled into the log2 domain
+      const bool all_full = __all_sync(0xffffffffu, full);
+      const bool pos = sc >= 0.f;
+      float ext = pos ? -INFINITY : INFINITY;
 #pragma unroll
-        for (int c = 0; c < kTcKeys; ++c) {
-          s[c] *= p.scale_log2;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
+      for (int c = 0; c < kTcKeys; c += 64) {
+        uint32_t raw[64];
+        tmem_ld64(sbuf + c, raw);
+        if (all_full) {
+          float e0 = ext, e1 = pos ? -INFINITY : INFINITY;
 #pragma unroll
-        for (int c = 0; c < kTcKeys; ++c) {
-          s[c] = (key0 + c < vis_end) ? s[c] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
+          for (int i = 0; i < 64; i += 2) {
+            e0 = pos ? fmaxf(e0, __uint_as_float(raw[i])) : fminf(e0, __uint_as_float(raw[i]));
+            e1 = pos ? fmaxf(e1, __uint_as_float(raw[i + 1])) : fminf(e1, __uint_as_float(raw[i + 1]));
+          }
+          ext = pos ? fmaxf(e0, e1) : fminf(e0, e1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float v = __uint_as_float(raw[i]);
+            const bool vis = key0 + c + i < vis_end;
+            ext = vis ? (pos ? fmaxf(ext, v) : fminf(ext, v)) : ext;
+          }
         }
       }
+      const float mx = (ext == INFINITY || ext == -INFINITY) ? -INFINITY : ext * sc;
       const bool grow = mx > m_run + kRescaleThreshold;
       float alpha = 1.f;
       if (grow) {
@@ -380,77 +473,113 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         m_run = mx;
         l_run *= alpha;
       }
-      float rs = 0.f;
-      uint32_t packed[kTcKeys / 2];
-      if (m_run == -INFINITY) {
-#pragma unroll
-        for (int c = 0; c < kTcKeys / 2; ++c) packed[c] = 0u;
-      } else {
-#pragma unroll
-        for (int c = 0; c < kTcKeys; c += 2) {
-          const float p0 = fast_exp2(s[c] - m_run);
-          const float p1 = fast_exp2(s[c + 1] - m_run);
-          rs += p0 + p1;
-          packed[c >> 1] = Elem<T>::pack(p0, p1);
-        }
-      }
-      l_run += rs;
-
-      // P buffer j%2 is free once P.V of tile j-2 finished; a rescale of O
-      // additionally needs P.V of tile j-1 finished (O must be at rest).
-      const bool warp_grow = __any_sync(0xffffffffu, grow) && j > 0;
-      if (warp_grow) {
-        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      // O_g last received P.V of tile j-2, which completed before S_j (same
+      // issuing thread), so it is at rest here; rescale it when a row max grew
+      if (__any_sync(0xffffffffu, grow) && j >= 2) {
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t o[32];
-          tmem_ld32(lane_base + Cfg::kTmemO + c, o);
+          tmem_ld32(o_base + c, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(lane_base + Cfg::kTmemO + c, o);
-        }
-      } else if (j >= 2) {
-        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv_done[sb], ((j - 2) >> 1) & 1, abort))) {
-          ok = false;
-          break;
+          tmem_st32(o_base + c, o);
         }
       }
-      const uint32_t pt = lane_base + Cfg::kTmemP + sb * 64;
-      tmem_st32(pt, *reinterpret_cast<const uint32_t(*)[32]>(&packed[0]));
-      tmem_st32(pt + 32, *reinterpret_cast<const uint32_t(*)[32]>(&packed[32]));
+
+      // pass 2: P = 2^(s*scale - m) over each 64-key half, packed in pairs into
+      // the 32 columns of S that the halves before it already consumed
+      float rs = 0.f;
+      const float neg_m = -m_run;
+      const bool live = m_run != -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTcKeys; c += 64) {
+        uint32_t raw[64];
+        tmem_ld64(sbuf + c, raw);
+        uint32_t packed[32];
+        if (all_full && live) {
+          float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m));
+            r0 += p0;
+            r1 += p1;
+            packed[i >> 1] = Elem<T>::pack(p0, p1);
+          }
+          rs += r0 + r1;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const bool v0 = live && key0 + c + i < vis_end;
+            const bool v1 = live && key0 + c + i + 1 < vis_end;
+            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
+            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
+            rs += p0 + p1;
+            packed[i >> 1] = Elem<T>::pack(p0, p1);
+          }
+        }
+        tmem_st32(sbuf + (c >> 1), packed);
+      }
+      l_run += rs;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[sb]);
+      if (lane == 0) mbar_arrive(&bars->p_full[g]);
     }
 
-    // epilogue: O / l
-    if (ok && __all_sync(0xffffffffu, tc_wait(&bars->pv_done[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, abort))) {
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
+    // ---------------------------------------------------------- merge + store
+    // Both accumulators must be complete; the last P.V is the last product,
+    // so afterwards the Q tile's shared memory is free for the (m, l) exchange.
+    bool done_ok = ok;
 #pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(lane_base + Cfg::kTmemO + c, o);
+    for (int gg = 0; gg < 2; ++gg) {
+      if (nkt > gg) {
+        const int jl = gg + ((nkt - 1 - gg) >> 1) * 2;  // last tile of parity gg
+        done_ok = __all_sync(0xffffffffu, done_ok && tc_wait(&bars->pv_done[gg], (jl >> 1) & 1, abort));
+      }
+    }
+    fence_proxy_async_smem();
+    ml[(g * 2) * kTcRows + r] = m_run;
+    ml[(g * 2 + 1) * kTcRows + r] = l_run;
+    named_barrier_sync(1, 2 * kTcGroupWarps * 32);
+    if (done_ok) {
+      tc_fence_after();
+      const float m0 = ml[r], l0 = ml[kTcRows + r];
+      const float m1 = ml[2 * kTcRows + r], l1 = ml[3 * kTcRows + r];
+      const float M = fmaxf(m0, m1);
+      const float a0 = m0 != -INFINITY ? fast_exp2(m0 - M) : 0.f;
+      const float a1 = m1 != -INFINITY ? fast_exp2(m1 - M) : 0.f;
+      const float L = l0 * a0 + l1 * a1;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const float w0 = a0 * inv, w1 = a1 * inv;
+      const bool two = nkt > 1;
+      T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
+      // group g stores columns [g*HD/2, (g+1)*HD/2)
+#pragma unroll
+      for (int c = g * (HD / 2); c < (g + 1) * (HD / 2); c += 32) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(lane_base + Cfg::kTmemO + c, o0);
+        if (two) tmem_ld32(lane_base + Cfg::kTmemO + HD + c, o1);
         if (qi < q_len) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float x0 = w0 > 0.f ? __uint_as_float(o0[i + e]) * w0 : 0.f;
+              const float x1 = (two && w1 > 0.f) ? __uint_as_float(o1[i + e]) * w1 : 0.f;
+              f[e] = x0 + x1;
+            }
             uint4 v;
-            v.x = Elem<T>::pack(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
-            v.y = Elem<T>::pack(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-            v.z = Elem<T>::pack(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-            v.w = Elem<T>::pack(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+            v.x = Elem<T>::pack(f[0], f[1]);
+            v.y = Elem<T>::pack(f[2], f[3]);
+            v.z = Elem<T>::pack(f[4], f[5]);
+            v.w = Elem<T>::pack(f[6], f[7]);
             *reinterpret_cast<uint4*>(orow + c + i) = v;
           }
         }
       }
-      if (qi < q_len && p.lse != nullptr)
-        p.lse[static_cast<size_t>(q_start + qi) * p.HQ + h] =
-            l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+      if (g == 0 && qi < q_len && p.lse != nullptr)
+        p.lse[static_cast<size_t>(q_start + qi) * p.HQ + h] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
     }
   }
 
