@@ -177,7 +177,20 @@ int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, 
   auto kern = paged_decode_kernel<T, HD, NT, kTma, kFp8>;
   const int smem = DecodeCfg<HD, NT, kFp8>::kSmemBytes;
   if (int rc = ensure_smem(kern, smem, done)) return rc;
-  kern<<<grid, kDecThreads, smem, st>>>(p, tk, tv);
+  // programmatic dependent launch (the kernel waits for its predecessor
+  // before reading inputs, and releases its successor early)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "paged_decode_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_kernel");
 }
 

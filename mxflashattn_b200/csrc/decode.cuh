@@ -208,6 +208,14 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + Cfg::kRingBytes);
   uint64_t* empty = full + Cfg::kSlots;
 
+  // Programmatic dependent launch: let the next kernel on the stream start
+  // placing its blocks as soon as every block of this grid is running (they
+  // fill SMs this grid's tail frees), and wait for the previous kernel to
+  // finish before touching any input.  Both are no-ops without the launch
+  // attribute.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // Grid: x = (KV head, row group), y = length rank, z = split.  The hardware
   // dispatches blocks in linear order, so mapping rank y to the y-th longest
   // sequence starts the longest work first (longest-processing-time order),
