@@ -91,9 +91,12 @@ def _lse_varlen(case, torch):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-root", default=os.environ.get("MXFA_REFERENCE_ROOT", "/root/reference"))
+    parser.add_argument("--reference-root", default=os.environ.get("MXFA_REFERENCE_ROOT"),
+                        help="checkout of the reference project (or set MXFA_REFERENCE_ROOT)")
     parser.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = parser.parse_args()
+    if not args.reference_root:
+        parser.error("--reference-root (or MXFA_REFERENCE_ROOT) is required")
     sys.path.insert(0, args.reference_root)
     import torch
     from mxflashattn import reference as ref  # the reference's own oracle
