@@ -214,6 +214,20 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
   // finish before touching any input.  Both are no-ops without the launch
   // attribute.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // set-up that reads no input overlaps the predecessor's tail: the slot
+  // barriers, and the tensor-map descriptors (kernel parameters) warmed for
+  // the producer's first copies
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kSlots; ++s) {
+      mbar_init(&full[s], kTma ? 1 : 32);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  if (kTma && threadIdx.x == kDecConsumerWarps * 32) {
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // Grid: x = (KV head, row group), y = length rank, z = split.  The hardware
@@ -327,24 +341,13 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < Cfg::kSlots; ++s) {
-      mbar_init(&full[s], kTma ? 1 : 32);
-      mbar_init(&empty[s], 1);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
+  __syncthreads();  // rank result, appended rows and slot barriers visible to every warp
 
   // ---------------------------------------------------------------- producer
   if (warp == kDecConsumerWarps) {
     const uint8_t* kc = static_cast<const uint8_t*>(p.k);
     const uint8_t* vc = static_cast<const uint8_t*>(p.v);
     if constexpr (kTma) {
-      if (lane == 0) {
-        prefetch_tensormap(&tmk);
-        prefetch_tensormap(&tmv);
-      }
       int abort = 0;
       int issued = 0;  // lane 0: tiles whose copies were started
       for (int base = 0; base < ntiles && !abort; base += 32) {
