@@ -168,6 +168,41 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
                                          int append_len, int num_splits, int chunk_len, int causal, int bf16,
                                          float scale, void* stream);
 
+/* ---- Context-parallel decode with the exchange fused over peer memory ----
+ * No reference counterpart (the reference runs on one device).  A group of
+ * `world` ranks (one process per GPU) each hold a contiguous range of every
+ * sequence's pages.  Per call:
+ *   mxfa_cp_decode_launch  split decode of the local range; the merging CTA of
+ *                          each (sequence, KV head) writes its normalised
+ *                          (O, LSE) record into EVERY rank's exchange buffer
+ *                          (plain NVLink stores) and raises a flag there;
+ *   mxfa_cp_merge_launch   on each rank: wait (bounded) for all ranks' flags,
+ *                          LSE-merge the records in rank order, write out /
+ *                          lse.
+ * This replaces the NCCL all-gather of the records.  Exchange buffers come
+ * from mxfa_peer_alloc (zeroed cudaMalloc) and are mapped on the other ranks
+ * with mxfa_peer_export / mxfa_peer_import (CUDA IPC; no multicast).  One
+ * buffer serves every layer: a device-side epoch advances per call and
+ * alternates two halves of the buffer.  All ranks must issue the same
+ * sequence of calls.  A rank that stops participating makes the others'
+ * merge time out after 1 s (MXFA_FLAG_WAIT_TIMEOUT). */
+size_t mxfa_cp_buffer_bytes(int world, int B, int HQ, int HKV, int D);
+int mxfa_peer_alloc(size_t bytes, void** ptr);
+int mxfa_peer_free(void* ptr);
+int mxfa_peer_export(void* ptr, void* handle /* 64 bytes */);
+int mxfa_peer_import(const void* handle /* 64 bytes */, void** ptr);
+int mxfa_peer_close(void* ptr);
+/* peer_bufs: device array of `world` exchange-buffer addresses as seen from
+ * this rank (entry `rank` is the local buffer).  counters: as in
+ * mxfa_kvcache_attention_counted_launch.  One query token per sequence. */
+int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                          const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                          unsigned int* counters, const unsigned long long* peer_bufs, int rank, int world, int B,
+                          int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits, int chunk_len,
+                          int bf16, float scale, void* stream);
+int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int B, int HQ, int HKV, int D, int bf16,
+                         void* stream);
+
 /* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
  * counterpart in the reference.  It exists for callers that cannot allocate
  * device memory when they run attention (an engine that pre-reserved all GPU

@@ -52,6 +52,16 @@ SIGNATURES = {
     "mxfa_kvcache_append_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _i, _i, _f, _vp]),
+    "mxfa_cp_buffer_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "mxfa_peer_alloc": (_i, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "mxfa_peer_free": (_i, [_vp]),
+    "mxfa_peer_export": (_i, [_vp, _vp]),
+    "mxfa_peer_import": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "mxfa_peer_close": (_i, [_vp]),
+    "mxfa_cp_decode_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _f, _vp]),
+    "mxfa_cp_merge_launch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "mxfa_kvcache_attention_noalloc_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "mxfa_kvcache_attention_packed_launch": (

@@ -125,3 +125,116 @@ def context_parallel_decode(q, k_cache, v_cache, local_seqlens, local_block_tabl
         out, lse = merged
         return out.reshape(B, 1, HQ, D), lse.reshape(B, HQ)
     return merged.reshape(B, 1, HQ, D)
+
+
+# ------------------------------------------------- fused exchange (peer memory)
+
+class FusedContextParallelDecode:
+    """Context-split decode with the (O, LSE) exchange fused into the kernels.
+
+    Same result as ``context_parallel_decode`` without the NCCL all-gather:
+    each rank's decode publishes its records straight into every rank's
+    exchange buffer over NVLink (plain stores to CUDA-IPC-mapped memory), and
+    a small merge kernel on each rank waits for all ranks' flags and merges.
+    One instance serves a fixed geometry (batch, heads, head dim) for any
+    number of calls and layers; every rank must make the same calls in the
+    same order.  ``close()`` (collective) releases the mappings.
+    """
+
+    def __init__(self, batch: int, q_heads: int, kv_heads: int, head_dim: int, *, group=None, device=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._lib = lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.geometry = (batch, q_heads, kv_heads, head_dim)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = int(lib.mxfa_cp_buffer_bytes(self.world, batch, q_heads, kv_heads, head_dim))
+        if nbytes == 0:
+            raise ValueError(f"unsupported context-parallel geometry {self.geometry}")
+        with torch.cuda.device(self.device):
+            local = ctypes.c_void_p()
+            _lib.check(lib.mxfa_peer_alloc(nbytes, ctypes.byref(local)), "mxfa_peer_alloc")
+            self._local = local.value
+            handle = (ctypes.c_char * 64)()
+            _lib.check(lib.mxfa_peer_export(self._local, handle), "mxfa_peer_export")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._imported = []
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._local)
+                    continue
+                buf = (ctypes.c_char * 64).from_buffer_copy(h)
+                peer = ctypes.c_void_p()
+                _lib.check(lib.mxfa_peer_import(buf, ctypes.byref(peer)), "mxfa_peer_import")
+                self._imported.append(peer.value)
+                ptrs.append(peer.value)
+            # device array of the peers' buffer addresses (uint64 stored as int64)
+            self.peer_table = torch.tensor([p - (1 << 64) if p >= (1 << 63) else p for p in ptrs],
+                                           dtype=torch.int64, device=self.device)
+        dist.barrier(group=group)
+
+    def __call__(self, q, k_cache, v_cache, local_seqlens, local_block_table, softmax_scale=None, *,
+                 num_splits: int = 0, chunk_len: int = 0, return_lse: bool = False):
+        import torch
+
+        from . import _lib, backend
+
+        B, Sq, HQ, D = q.shape
+        if (B, HQ, k_cache.shape[2], D) != self.geometry or Sq != 1:
+            raise ValueError(f"call geometry {(B, HQ, k_cache.shape[2], D)} (Sq={Sq}) does not match "
+                             f"{self.geometry} with one query token")
+        scale = softmax_scale if softmax_scale is not None else D ** -0.5
+        q = q.contiguous()
+        seq = local_seqlens.to(torch.int32).contiguous()
+        bt = local_block_table.to(torch.int32).contiguous()
+        PS, HKV = k_cache.shape[1], k_cache.shape[2]
+        btw = bt.shape[1]
+        if num_splits <= 0 or chunk_len <= 0:
+            num_splits, chunk_len = backend.kvcache_plan(B, 1, HQ, HKV, D, btw * PS)
+        lib = self._lib
+        ws_bytes = int(lib.mxfa_split_workspace_bytes(B * HQ, D, num_splits))
+        out = torch.empty_like(q)
+        lse = torch.empty((B, HQ), device=q.device, dtype=torch.float32) if return_lse else None
+        with torch.cuda.device(q.device):
+            stream = torch.cuda.current_stream(q.device).cuda_stream
+            ws = torch.empty((max(ws_bytes, 16) // 4,), device=q.device, dtype=torch.float32)
+            counters = backend.split_counters(q.device, stream, int(lib.mxfa_split_counter_bytes(B, 1, HQ, HKV)))
+            bf16 = int(q.dtype == torch.bfloat16)
+            rc = lib.mxfa_cp_decode_launch(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), seq.data_ptr(),
+                out.data_ptr(), None, ws.data_ptr(), ws_bytes, counters.data_ptr(), self.peer_table.data_ptr(),
+                self.rank, self.world, B, HQ, HKV, D, PS, btw, k_cache.shape[0], num_splits, chunk_len, bf16,
+                float(scale), stream)
+            _lib.check(rc, "mxfa_cp_decode_launch")
+            rc = lib.mxfa_cp_merge_launch(self._local, out.data_ptr(), _lib.ptr(lse), self.world, B, HQ, HKV, D,
+                                          bf16, stream)
+            _lib.check(rc, "mxfa_cp_merge_launch")
+        return (out, lse) if return_lse else out
+
+    def close(self) -> None:
+        """Collective: every rank stops using the buffers, then mappings and memory are released."""
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if self._local is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._imported:
+                _lib.check(self._lib.mxfa_peer_close(p), "mxfa_peer_close")
+            self._imported = []
+            dist.barrier(group=self.group)  # no rank still maps this rank's buffer
+            _lib.check(self._lib.mxfa_peer_free(self._local), "mxfa_peer_free")
+        self._local = None

@@ -512,6 +512,140 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
                                 bf16, scale, k_new, v_new, counters, stream);
 }
 
+// ------------------------------------------------ context-parallel exchange
+
+size_t mxfa_cp_buffer_bytes(int world, int B, int HQ, int HKV, int D) {
+  if (world <= 0 || B <= 0 || HKV <= 0 || HQ <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return 0;
+  return cp_layout(world, B * HKV, B * HQ, D).bytes;
+}
+
+int mxfa_peer_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return fail(MXFA_ERR_INVALID, "bad peer allocation request");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return fail(MXFA_ERR_CUDA, "peer buffer allocation: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return MXFA_OK;
+}
+
+int mxfa_peer_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? MXFA_OK : fail(MXFA_ERR_CUDA, "peer buffer free: %s", cudaGetErrorString(e));
+}
+
+int mxfa_peer_export(void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr) return fail(MXFA_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "IPC export: %s", cudaGetErrorString(e));
+  std::memcpy(handle, &h, sizeof(h));
+  return MXFA_OK;
+}
+
+int mxfa_peer_import(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(MXFA_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "IPC import: %s", cudaGetErrorString(e));
+  *ptr = p;
+  return MXFA_OK;
+}
+
+int mxfa_peer_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? MXFA_OK : fail(MXFA_ERR_CUDA, "IPC close: %s", cudaGetErrorString(e));
+}
+
+int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                          const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                          unsigned* counters, const unsigned long long* peer_bufs, int rank, int world, int B,
+                          int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits, int chunk_len,
+                          int bf16, float scale, void* stream) {
+  if (peer_bufs == nullptr || counters == nullptr) return fail(MXFA_ERR_INVALID, "peer buffers / counters missing");
+  if (world < 1 || world > 32 || rank < 0 || rank >= world)
+    return fail(MXFA_ERR_INVALID, "rank %d of world %d (1..32 ranks)", rank, world);
+  if (HKV <= 0 || HQ % HKV != 0 || HQ / HKV > 16)
+    return fail(MXFA_ERR_UNSUPPORTED, "context-parallel decode covers up to 16 query heads per KV head");
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (B <= 0) return MXFA_OK;
+  const int max_len = block_table ? BTW * PS : PS;
+  if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, 1, HQ, HKV, D, max_len, &num_splits, &chunk_len);
+  const long long rows = static_cast<long long>(B) * HQ;
+  const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
+  if (static_cast<long long>(num_splits) * chunk_len < max_len)
+    return fail(MXFA_ERR_INVALID, "%d splits of %d positions do not cover the cache capacity %d", num_splits,
+                chunk_len, max_len);
+  if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  DecodeParams p{};
+  p.q = q;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.bt = block_table;
+  p.seqlens = seqlens;
+  p.out = out;
+  p.lse = lse;
+  p.B = B;
+  p.Sq = 1;
+  p.HQ = HQ;
+  p.HKV = HKV;
+  p.PS = PS;
+  p.BTW = block_table ? BTW : 1;
+  p.P = num_pages;
+  p.GQ = HQ / HKV;
+  p.causal = 0;
+  p.scale_log2 = scale * kLog2e;
+  p.v_scale = 1.f;
+  p.NP = num_splits;
+  p.c_len = chunk_len;
+  p.ows = static_cast<float*>(workspace);
+  p.mdws = p.ows + rows * num_splits * D;
+  p.counters = counters;
+  p.cp_bufs = peer_bufs;
+  p.cp_rank = rank;
+  p.cp_world = world;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return run_decode(p, D, bf16 != 0, st);
+}
+
+int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int B, int HQ, int HKV, int D, int bf16,
+                         void* stream) {
+  if (local_buf == nullptr || out == nullptr) return fail(MXFA_ERR_INVALID, "null pointer");
+  if (world < 1 || HKV <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return fail(MXFA_ERR_INVALID, "bad geometry");
+  if (B <= 0) return MXFA_OK;
+  const int rows = B * HQ;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((rows + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto* buf = static_cast<unsigned char*>(local_buf);
+  cudaError_t e;
+  if (bf16)
+    e = D == 128 ? cudaLaunchKernelEx(&cfg, cp_merge_kernel<__nv_bfloat16, 128>, buf,
+                                      static_cast<__nv_bfloat16*>(out), lse, rows, HQ, HQ / HKV, world, B * HKV)
+                 : cudaLaunchKernelEx(&cfg, cp_merge_kernel<__nv_bfloat16, 64>, buf,
+                                      static_cast<__nv_bfloat16*>(out), lse, rows, HQ, HQ / HKV, world, B * HKV);
+  else
+    e = D == 128 ? cudaLaunchKernelEx(&cfg, cp_merge_kernel<__half, 128>, buf, static_cast<__half*>(out), lse, rows,
+                                      HQ, HQ / HKV, world, B * HKV)
+                 : cudaLaunchKernelEx(&cfg, cp_merge_kernel<__half, 64>, buf, static_cast<__half*>(out), lse, rows,
+                                      HQ, HQ / HKV, world, B * HKV);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "cp_merge_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("cp_merge_kernel");
+}
+
 int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt, const void* sl,
                                    void* out, void* ows, void* mdws, float scale, int B, int HQ, int HKV, int D,
                                    int PS, int BTW, int bf16, int NP, int c_len, int um, void* stream) {

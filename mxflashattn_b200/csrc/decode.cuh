@@ -58,6 +58,12 @@ struct DecodeParams {
   // FP8 (e4m3) caches: dequantised value = stored * scale.  k_scale is folded
   // into scale_log2 by the launcher; v_scale multiplies the output.
   float v_scale;
+  // Context-parallel exchange (optional, with counters): instead of writing
+  // out / lse, the merging CTA of a unit publishes its (O, LSE) record into
+  // the exchange buffer of every rank (peer memory) and raises its flag
+  // there; cp_merge_kernel on each rank completes the merge.
+  const unsigned long long* cp_bufs;  // [cp_world] exchange-buffer bases; [cp_rank] is local
+  int cp_rank, cp_world;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -125,6 +131,36 @@ __device__ __forceinline__ int tile_slot_row(const DecodeParams& p, int b, int t
     phys = p.P;
   }
   return phys * p.PS + (pos % p.PS);
+}
+
+// Exchange buffer of a context-parallel group (one per rank, allocated zeroed;
+// peers map it through CUDA IPC).  Every step (call) advances a device-side
+// epoch e and uses half e % 2 of the flags and records, so a rank that is one
+// step ahead never overwrites what a slower rank still reads:
+//   [0, 256)   header: epoch (u32), blocks done (u32)
+//   flags      [2][world][units] u32: flag[e%2][src][unit] = e + 1 once rank
+//              src published that unit's records for step e
+//   records    [2][world][rows][D + 1] f32: normalised O then natural-log LSE
+struct CpLayout {
+  size_t flags, flag_half, records, record_half, bytes;
+};
+__host__ __device__ inline CpLayout cp_layout(int world, int units, int rows, int D) {
+  CpLayout l;
+  l.flags = 256;
+  l.flag_half = static_cast<size_t>(world) * units * 4;
+  l.records = (l.flags + 2 * l.flag_half + 255) / 256 * 256;
+  l.record_half = static_cast<size_t>(world) * rows * (D + 1) * 4;
+  l.bytes = l.records + 2 * l.record_half;
+  return l;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Merge the NP split partials of query row r (one warp; lanes own HD/32
@@ -196,6 +232,57 @@ __device__ __forceinline__ void merge_split_row(const float* ows, const float* m
 
 // kFp8: e4m3 caches.  Tiles are dequantised in registers (cvt e4m3x2 ->
 // f16x2, exact) and both products run in f16; q is converted to f16 once.
+// merge_split_row for the exchange: the normalised f32 row and its LSE are
+// written to the record slot [cp_rank][r] of every rank's exchange buffer.
+template <int HD>
+__device__ __forceinline__ void merge_split_row_publish(const float* ows, const float* mdws, int r, int NP,
+                                                        int lane, const unsigned long long* bufs, int world,
+                                                        int rank, int rows, size_t rec_off) {
+  constexpr int kPer = HD / 32;
+  const float* md = mdws + static_cast<size_t>(r) * NP * 2;
+  float M = -INFINITY;
+  for (int pz = lane; pz < NP; pz += 32) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+    if (v.x > -INFINITY && v.y > 0.f) M = fmaxf(M, v.x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (int pz = lane; pz < NP; pz += 32) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+      if (v.x > -INFINITY && v.y > 0.f) L += v.y * fast_exp2(v.x - M);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  if (M != -INFINITY) {
+    const float* src = ows + static_cast<size_t>(r) * NP * HD + lane * kPer;
+#pragma unroll 8
+    for (int pz = 0; pz < NP; ++pz) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
+      const bool valid = v.x > -INFINITY && v.y > 0.f;
+      const float w = fast_exp2(v.x - M);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const float o = __ldcg(src + static_cast<size_t>(pz) * HD + j);
+        acc[j] = valid ? fmaf(w, o, acc[j]) : acc[j];
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const float lse = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  for (int dst = 0; dst < world; ++dst) {
+    float* rec = reinterpret_cast<float*>(bufs[dst] + rec_off) + (static_cast<size_t>(rank) * rows + r) * (HD + 1);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) rec[lane * kPer + j] = acc[j] * inv;
+    if (lane == 0) rec[HD] = lse;
+  }
+}
+
 template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
 __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPerSm)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
@@ -770,13 +857,31 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
     named_barrier_sync(1, kDecConsumerWarps * 32);
     if (s_last) {
       __threadfence();
+      const int rows_all = p.B * p.Sq * p.HQ;
+      const CpLayout lay = cp_layout(p.cp_world, p.B * gridDim.x, rows_all, HD);
+      const unsigned epoch =
+          p.cp_bufs != nullptr ? *reinterpret_cast<const volatile unsigned*>(p.cp_bufs[p.cp_rank]) : 0u;
       for (int col = warp; col < Mg::kCols; col += kDecConsumerWarps) {
         const int rr = row_base + col;
         if (rr >= rows_total) break;
         const int i = rr / p.GQ;
         const int h = kvh * p.GQ + rr % p.GQ;
         const int R = (b * p.Sq + i) * p.HQ + h;
-        merge_split_row<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
+        if (p.cp_bufs != nullptr)
+          merge_split_row_publish<HD>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank, rows_all,
+                                      lay.records + (epoch & 1u) * lay.record_half);
+        else
+          merge_split_row<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
+      }
+      if (p.cp_bufs != nullptr) {
+        // every writer's records reach every rank before its flag does
+        __threadfence_system();
+        named_barrier_sync(1, kDecConsumerWarps * 32);
+        if (tid < p.cp_world) {
+          const unsigned unit = static_cast<unsigned>(b) * gridDim.x + blockIdx.x;
+          unsigned* flags = reinterpret_cast<unsigned*>(p.cp_bufs[tid] + lay.flags + (epoch & 1u) * lay.flag_half);
+          st_release_sys(flags + static_cast<size_t>(p.cp_rank) * p.B * gridDim.x + unit, epoch + 1u);
+        }
       }
       if (tid == 0) *counter = 0u;  // ready for the next launch on this stream
     }
@@ -856,6 +961,70 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const float* __restr
       for (int j = 0; j < kPer; ++j) out_f32[static_cast<size_t>(r) * HD + lane * kPer + j] = acc[j] * inv;
     }
     if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  }
+}
+
+// ------------------------------------------------ context-parallel merge
+
+// One warp per query row on each rank: wait (bounded) until every rank's
+// flag for the row's unit shows this step, then LSE-merge the world records
+// of the row in rank order (the algebra of the packed merge above) and write
+// the output.  The last block to finish advances the epoch.
+template <typename T, int HD>
+__global__ void __launch_bounds__(128) cp_merge_kernel(unsigned char* buf, T* __restrict__ out,
+                                                       float* __restrict__ lse, int rows, int HQ, int GQ, int world,
+                                                       int units) {
+  constexpr int kPer = HD / 32;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  unsigned* hdr = reinterpret_cast<unsigned*>(buf);
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(hdr);
+  const CpLayout lay = cp_layout(world, units, rows, HD);
+  if (r < rows) {
+    // row r = b * HQ + h belongs to unit (b, h / GQ); units are numbered b * (HQ / GQ) + h / GQ
+    const int unit = (r / HQ) * (HQ / GQ) + (r % HQ) / GQ;
+    const unsigned* flags = reinterpret_cast<const unsigned*>(buf + lay.flags + (epoch & 1u) * lay.flag_half);
+    bool ready = lane >= world;
+    const unsigned long long t0 = global_timer_ns();
+    while (!__all_sync(0xffffffffu, ready)) {
+      if (!ready) ready = ld_acquire_sys(flags + static_cast<size_t>(lane) * units + unit) == epoch + 1u;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (lane == 0) raise_flag(MXFA_FLAG_WAIT_TIMEOUT);
+        break;
+      }
+    }
+    __syncwarp();  // each lane acquired one rank's flag; the warp barrier shares what they saw
+    const float* recs = reinterpret_cast<const float*>(buf + lay.records + (epoch & 1u) * lay.record_half);
+    float M = -INFINITY, L = 0.f;
+    float acc[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+    for (int src = 0; src < world; ++src) {
+      const float* rec = recs + (static_cast<size_t>(src) * rows + r) * (HD + 1);
+      const float mz = __ldcg(rec + HD) * kLog2e;  // (O, lse) == (o = O, m = lse*log2e, d = 1)
+      if (!(mz > -INFINITY)) continue;
+      const float mn = fmaxf(M, mz);
+      const float f1 = fast_exp2(M - mn);
+      const float f2 = fast_exp2(mz - mn);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) acc[j] = acc[j] * f1 + __ldcg(rec + lane * kPer + j) * f2;
+      L = L * f1 + f2;
+      M = mn;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
+#pragma unroll
+    for (int j = 0; j < kPer; j += 2) *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
+    if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(hdr + 1, 1u) == gridDim.x - 1) {
+      hdr[1] = 0u;
+      *reinterpret_cast<volatile unsigned*>(hdr) = epoch + 1u;
+    }
   }
 }
 

@@ -78,6 +78,100 @@ def _nccl_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
+def _fused_worker(rank, world, port, result):
+    """Fused exchange vs the NCCL path and the oracle, over three calls (both buffer halves)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    fused = None
+    try:
+        from mxflashattn_b200 import _lib
+
+        case = _case()
+        tdt = syn.torch_dtype(case.dtype)
+        dev = torch.device("cuda", rank)
+        ll, table = cs.local_view(case.cache_seqlens, case.block_table, world, rank, 16)
+        kc = torch.from_numpy(case.k_cache).to(dev, tdt)
+        vc = torch.from_numpy(case.v_cache).to(dev, tdt)
+        sl = torch.from_numpy(ll).to(dev)
+        bt = torch.from_numpy(table).to(dev)
+        fused = cs.FusedContextParallelDecode(4, 32, 8, 128, device=dev)
+        worst = -1.0
+        for step in range(3):
+            q_np = case.q if step == 0 else syn.round_dtype(np.random.default_rng(50 + step).standard_normal(
+                case.q.shape).astype(np.float32), "bf16")
+            q = torch.from_numpy(q_np).to(dev, tdt)
+            out, lse = fused(q, kc, vc, sl, bt, case.softmax_scale, return_lse=True)
+            nccl = cs.context_parallel_decode(q, kc, vc, sl, bt, case.softmax_scale)
+            torch.cuda.synchronize()
+            import dataclasses
+
+            ref, ref_lse = oracle_paged(dataclasses.replace(case, q=q_np))[:2]
+            worst = max(worst, float(np.max(np.abs(host(out) - ref) - out_tolerance(ref, "bf16"))))
+            worst = max(worst, float(np.max(np.abs(host(out) - host(nccl)) - out_tolerance(ref, "bf16"))))
+            lse_err = float(np.max(np.abs(host(lse).reshape(4, 1, 32) - ref_lse)))
+            worst = max(worst, lse_err - 1e-3)
+        result[rank] = worst  # <= 0 when every element is within tolerance
+        result[f"flags{rank}"] = int(_lib.read_error_flags())
+    finally:
+        if fused is not None:
+            fused.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_fused_peer_exchange(cuda_device):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    manager = mp.Manager()
+    result = manager.dict()
+    mp.spawn(_fused_worker, args=(2, port, result), nprocs=2, join=True)
+    assert all(result[r] <= 0.0 for r in range(2)), dict(result)
+    assert all(result[f"flags{r}"] == 0 for r in range(2)), dict(result)
+
+
+def test_single_rank_fused_exchange_matches_local_decode(cuda_device):
+    """world = 1: the exchange degenerates to the local record (no peer, no waiting on another device)."""
+    import datetime as _dt
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=_dt.timedelta(seconds=60))
+    try:
+        case = _case()
+        tdt = syn.torch_dtype(case.dtype)
+        q = torch.from_numpy(case.q).to(cuda_device, tdt)
+        kc = torch.from_numpy(case.k_cache).to(cuda_device, tdt)
+        vc = torch.from_numpy(case.v_cache).to(cuda_device, tdt)
+        sl = torch.from_numpy(case.cache_seqlens.copy()).to(cuda_device)
+        bt = torch.from_numpy(case.block_table).to(cuda_device)
+        fused = cs.FusedContextParallelDecode(4, 32, 8, 128, device=cuda_device)
+        try:
+            ref = oracle_paged(case)[0]
+            for _ in range(3):
+                out = fused(q, kc, vc, sl, bt, case.softmax_scale)
+                torch.cuda.synchronize()
+                assert_close_out(host(out), ref, "bf16", "single-rank fused exchange")
+        finally:
+            fused.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def test_two_gpu_nccl_context_split(cuda_device):
     import torch
     import torch.multiprocessing as mp
