@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
                     help="decode: config 2 (headline); prefill: config 5 varlen causal forward")
     ap.add_argument("--prefill-lens", default="15000,1024,512,37")
+    ap.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
+                    help="decode KV cache type (fp8 = float8_e4m3fn at scale 1; bytes counted at 1 B/element)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -239,12 +241,16 @@ def run_ours(args):
 
     lengths = syn.qwen3_4b_lengths(args.seed + rank, args.batch)
     layers = []
+    fp8 = args.kv_dtype == "fp8"
     for layer in range(args.layers):
-        layers.append(syn.device_paged_decode(seed=1000 * (rank + 1) + layer, lengths=lengths, q_heads=HQ,
-                                              kv_heads=HKV, head_dim=D, dtype="bf16", page_size=PS,
-                                              device=device))
+        t = syn.device_paged_decode(seed=1000 * (rank + 1) + layer, lengths=lengths, q_heads=HQ, kv_heads=HKV,
+                                    head_dim=D, dtype="bf16", page_size=PS, device=device)
+        if fp8:  # e4m3 caches at scale 1 (N(0,1) values fit the e4m3 range)
+            t["k_cache"] = t["k_cache"].to(torch.float8_e4m3fn)
+            t["v_cache"] = t["v_cache"].to(torch.float8_e4m3fn)
+        layers.append(t)
     torch.cuda.synchronize(device)
-    bytes_layer = syn.kv_bytes(lengths, HKV, D)
+    bytes_layer = syn.kv_bytes(lengths, HKV, D, elem_bytes=1 if fp8 else 2)
     bytes_step = bytes_layer * args.layers
     max_len = layers[0]["block_table"].shape[1] * PS
     num_splits, chunk_len = backend.kvcache_plan(args.batch, 1, HQ, HKV, D, max_len)
@@ -401,8 +407,8 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
+        "vs_baseline": None, "dtype": "bf16 (e4m3 KV cache)" if fp8 else "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD + (", e4m3 KV cache" if fp8 else ""), "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
                    "head_dim": D, "page_size": PS, "mean_ctx": float(sum(lengths)) / len(lengths),
                    "num_splits": num_splits, "chunk_len": chunk_len,
                    "l2": f"inputs larger than L2: {args.layers} distinct layer caches, "
@@ -411,7 +417,8 @@ def run_ours(args):
         "tok_per_s": tok_s,
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get((args.batch, args.seed)),
+                     "frac": achieved / peak,
+                     "traffic": None if fp8 else NCU_TRAFFIC_BYTES.get((args.batch, args.seed)),
                      "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "paged_decode_kernel" + (" + split_combine_kernel" if num_splits > 1 else ""),
                      "bytes_per_launch": bytes_layer, "avg_launch_ms": per_launch_ms},

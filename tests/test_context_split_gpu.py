@@ -185,3 +185,39 @@ def test_two_gpu_nccl_context_split(cuda_device):
     result = manager.dict()
     mp.spawn(_nccl_worker, args=(2, port, result), nprocs=2, join=True)
     assert all(result[r] <= 0.0 for r in range(2)), dict(result)
+
+
+def test_exchange_wait_times_out_and_reports(cuda_device):
+    """A merge whose peer never publishes gives up after its bounded wait and raises the timeout flag.
+
+    The exchange buffer is sized for two ranks but only this process exists, so
+    rank 1's flags are never set: every warp waits ~1 s, then the kernel
+    finishes, the context stays usable and the host reads the flag.
+    """
+    import ctypes
+    import time
+
+    import torch
+
+    from mxflashattn_b200 import _lib
+
+    lib = _lib.load()
+    B, HQ, HKV, D = 1, 8, 2, 128
+    nbytes = int(lib.mxfa_cp_buffer_bytes(2, B, HQ, HKV, D))
+    buf = ctypes.c_void_p()
+    _lib.check(lib.mxfa_peer_alloc(nbytes, ctypes.byref(buf)), "mxfa_peer_alloc")
+    try:
+        out = torch.empty((B * HQ, D), device=cuda_device, dtype=torch.bfloat16)
+        _lib.read_error_flags()
+        t0 = time.time()
+        _lib.check(lib.mxfa_cp_merge_launch(buf, out.data_ptr(), None, 2, B, HQ, HKV, D, 1,
+                                            torch.cuda.current_stream().cuda_stream), "mxfa_cp_merge_launch")
+        torch.cuda.synchronize()
+        waited = time.time() - t0
+        assert _lib.read_error_flags() & 4  # MXFA_FLAG_WAIT_TIMEOUT
+        assert 0.5 < waited < 30.0
+        # the device still works
+        x = torch.ones(4, device=cuda_device)
+        assert float((x * 2).sum()) == 8.0
+    finally:
+        _lib.check(lib.mxfa_peer_free(buf), "mxfa_peer_free")
