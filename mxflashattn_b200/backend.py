@@ -16,6 +16,8 @@ stream and reads nothing back to the host.
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from . import _lib
@@ -26,16 +28,21 @@ SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
 _AVAILABLE: dict[int, bool] = {}
 
 
+_CUDA_OK: list[bool] = []
+
+
 def is_available() -> bool:
     """True when the current CUDA device is sm_100 and the library is usable (cached per device)."""
-    if not torch.cuda.is_available():
-        return False
+    if not _CUDA_OK:
+        if not torch.cuda.is_available():
+            return False
+        _CUDA_OK.append(True)
     dev = torch.cuda.current_device()
     cached = _AVAILABLE.get(dev)
     if cached is not None:
         return cached
     try:
-        ok = bool(_lib.load().mxfa_is_available())
+        ok = bool(_L().mxfa_is_available())
     except _lib.NativeLibraryError:
         ok = False
     _AVAILABLE[dev] = ok
@@ -58,6 +65,25 @@ def _contig(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
 
+_NULL_CTX = contextlib.nullcontext()
+
+
+def _on(t: torch.Tensor):
+    """Device context for a launch: a no-op when ``t`` already lives on the current device."""
+    idx = t.device.index
+    return _NULL_CTX if idx == torch.cuda.current_device() else torch.cuda.device(idx)
+
+
+_LIB: list = []
+
+
+def _L():
+    """The loaded library (cached)."""
+    if not _LIB:
+        _LIB.append(_lib.load())
+    return _LIB[0]
+
+
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
@@ -72,8 +98,8 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     lse = torch.empty((q.shape[0], q.shape[1]), device=q.device, dtype=torch.float32) if return_lse else None
     cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
     batch = cu_q.numel() - 1
-    with torch.cuda.device(q.device):
-        rc = _lib.load().mxfa_varlen_fwd_launch(
+    with _on(q):
+        rc = _L().mxfa_varlen_fwd_launch(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_q.data_ptr(), cu_k.data_ptr(), out.data_ptr(),
             _lib.ptr(lse), batch, int(max_seqlen_q), int(max_seqlen_k), q.shape[0], k.shape[0], q.shape[1],
             k.shape[1], q.shape[2], int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
@@ -87,8 +113,8 @@ def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False)
     out = torch.empty_like(q)
     B, Sq, HQ, D = q.shape
     lse = torch.empty((B, Sq, HQ), device=q.device, dtype=torch.float32) if return_lse else None
-    with torch.cuda.device(q.device):
-        rc = _lib.load().mxfa_varlen_fwd_launch(
+    with _on(q):
+        rc = _L().mxfa_varlen_fwd_launch(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None, out.data_ptr(), _lib.ptr(lse), B, Sq,
             k.shape[1], B * Sq, B * k.shape[1], HQ, k.shape[2], D, int(bool(causal)), _bf16(q),
             float(softmax_scale), _stream(q))
@@ -105,12 +131,12 @@ def kvcache_plan(batch: int, q_len: int, q_heads: int, kv_heads: int, head_dim: 
     """(num_splits, chunk_len) the library picks for this shape on the current device (cached)."""
     import ctypes
 
-    key = (torch.cuda.current_device() if torch.cuda.is_available() else -1, batch, q_len, q_heads, kv_heads,
-           head_dim, max_len)
+    key = (torch.cuda.current_device() if (_CUDA_OK or torch.cuda.is_available()) else -1, batch, q_len, q_heads,
+           kv_heads, head_dim, max_len)
     plan = _PLANS.get(key)
     if plan is None:
         np_, cl = ctypes.c_int(0), ctypes.c_int(0)
-        _lib.check(_lib.load().mxfa_kvcache_plan(batch, q_len, q_heads, kv_heads, head_dim, max_len,
+        _lib.check(_L().mxfa_kvcache_plan(batch, q_len, q_heads, kv_heads, head_dim, max_len,
                                                   ctypes.byref(np_), ctypes.byref(cl)), "mxfa_kvcache_plan")
         plan = _PLANS[key] = (int(np_.value), int(cl.value))
     return plan
@@ -165,7 +191,7 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
     if out is None:
         out = torch.empty_like(q)
     lse = torch.empty((B, Sq, HQ), device=q.device, dtype=torch.float32) if return_lse else None
-    lib = _lib.load()
+    lib = _L()
     if num_splits <= 0 or chunk_len <= 0:
         num_splits, chunk_len = kvcache_plan(B, Sq, HQ, HKV, D, max_len)
     ws = None
@@ -173,7 +199,7 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
     if num_splits > 1:
         ws_bytes = int(lib.mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits))
         ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
-    with torch.cuda.device(q.device):
+    with _on(q):
         stream = _stream(q)
         counters = None
         if num_splits > 1 and single_launch:
@@ -234,8 +260,8 @@ def kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table) -> None:
     seq = _i32(cache_seqlens)
     bt = None if block_table is None else _i32(block_table)
     B, Sk, HKV, D = k.shape
-    with torch.cuda.device(k.device):
-        rc = _lib.load().mxfa_kv_append_launch(
+    with _on(k):
+        rc = _L().mxfa_kv_append_launch(
             k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), B,
             Sk, HKV, D, k_cache.shape[1], 0 if bt is None else bt.shape[1], k_cache.shape[0], k.element_size(),
             _stream(k))
@@ -247,8 +273,8 @@ def seqlens_add_(cache_seqlens: torch.Tensor, delta: int) -> None:
     if cache_seqlens.dtype not in (torch.int32, torch.int64) or not cache_seqlens.is_contiguous():
         cache_seqlens.add_(delta)
         return
-    with torch.cuda.device(cache_seqlens.device):
-        rc = _lib.load().mxfa_seqlens_add_launch(
+    with _on(cache_seqlens):
+        rc = _L().mxfa_seqlens_add_launch(
             cache_seqlens.data_ptr(), int(cache_seqlens.dtype == torch.int64), cache_seqlens.numel(), int(delta),
             _stream(cache_seqlens))
     _lib.check(rc, "mxfa_seqlens_add_launch")
@@ -301,12 +327,12 @@ def kvcache_attention_packed(q, k_cache, v_cache, cache_seqlens, block_table, so
     max_len = btw * PS if bt is not None else PS
     if num_splits <= 0 or chunk_len <= 0:
         num_splits, chunk_len = kvcache_plan(B, 1, HQ, HKV, D, max_len)
-    lib = _lib.load()
+    lib = _L()
     ws_bytes = int(lib.mxfa_split_workspace_bytes(B * HQ, D, num_splits))
     ws = torch.empty((max(ws_bytes, 16) // 4,), device=q.device, dtype=torch.float32)
     if out is None:
         out = torch.empty((B * HQ, D + 1), device=q.device, dtype=torch.float32)
-    with torch.cuda.device(q.device):
+    with _on(q):
         rc = lib.mxfa_kvcache_attention_packed_launch(
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), out.data_ptr(),
             ws.data_ptr(), ws_bytes, B, HQ, HKV, D, PS, btw, k_cache.shape[0], num_splits, chunk_len, _bf16(q),
@@ -323,8 +349,8 @@ def split_combine(ows, mdws, rows: int, head_dim: int, num_splits: int, dtype, *
     if out is None:
         out = torch.empty((rows, head_dim), device=ows.device, dtype=dtype)
     lse_t = torch.empty((rows,), device=ows.device, dtype=torch.float32) if lse else None
-    with torch.cuda.device(ows.device):
-        rc = _lib.load().mxfa_split_combine_launch(
+    with _on(ows):
+        rc = _L().mxfa_split_combine_launch(
             ows.data_ptr(), mdws.data_ptr(), out.data_ptr(), None, _lib.ptr(lse_t), rows, head_dim, num_splits,
             int(dtype == torch.bfloat16), _stream(ows))
     _lib.check(rc, "mxfa_split_combine_launch")
@@ -337,8 +363,8 @@ def lse_merge(packed, rows: int, head_dim: int, dtype, *, lse: bool = False, out
     if out is None:
         out = torch.empty((rows, head_dim), device=packed.device, dtype=dtype)
     lse_t = torch.empty((rows,), device=packed.device, dtype=torch.float32) if lse else None
-    with torch.cuda.device(packed.device):
-        rc = _lib.load().mxfa_lse_merge_launch(
+    with _on(packed):
+        rc = _L().mxfa_lse_merge_launch(
             packed.data_ptr(), out.data_ptr(), _lib.ptr(lse_t), n_ranks, rows, head_dim,
             int(dtype == torch.bfloat16), _stream(packed))
     _lib.check(rc, "mxfa_lse_merge_launch")

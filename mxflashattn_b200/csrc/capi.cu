@@ -238,6 +238,57 @@ bool encode_kv_map_fp8(CUtensorMap* map, const void* k, const void* v, int HKV, 
   return true;
 }
 
+// Encoded K/V tensor maps of recently used caches, keyed by everything the
+// encoding reads (addresses, head dim, heads, slot rows, element type), so a
+// decode call reuses them instead of re-encoding (one driver call each).  A
+// small fixed table per device with round-robin replacement.
+struct KvMaps {
+  CUtensorMap tk{}, tv{};
+  int kind = 0, swap = 0;
+  bool tma = false;
+};
+struct KvMapEntry {
+  int device = -1;
+  const void *k = nullptr, *v = nullptr;
+  int D = 0, HKV = 0;
+  long long slots = 0;
+  bool fp8 = false;
+  KvMaps maps;
+};
+constexpr int kKvMapCache = 64;
+std::mutex g_kv_map_mu;
+KvMapEntry g_kv_maps[kKvMapCache];
+int g_kv_map_next = 0;
+
+bool kv_map_cache_get(const void* k, const void* v, int D, int HKV, long long slots, bool fp8, KvMaps* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_kv_map_mu);
+  for (const KvMapEntry& e : g_kv_maps) {
+    if (e.device == dev && e.k == k && e.v == v && e.D == D && e.HKV == HKV && e.slots == slots && e.fp8 == fp8) {
+      *out = e.maps;
+      return true;
+    }
+  }
+  return false;
+}
+
+void kv_map_cache_put(const void* k, const void* v, int D, int HKV, long long slots, bool fp8, const KvMaps& maps) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(g_kv_map_mu);
+  KvMapEntry& e = g_kv_maps[g_kv_map_next];
+  g_kv_map_next = (g_kv_map_next + 1) % kKvMapCache;
+  e.device = dev;
+  e.k = k;
+  e.v = v;
+  e.D = D;
+  e.HKV = HKV;
+  e.slots = slots;
+  e.fp8 = fp8;
+  e.maps = maps;
+}
+
 // Runs the decode kernel (split or direct) for a validated configuration;
 // kv_fp8: the caches hold e4m3 (D = 128 only).
 int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st, bool kv_fp8 = false) {
@@ -251,28 +302,38 @@ int run_decode(DecodeParams p, int D, bool bf16, cudaStream_t st, bool kv_fp8 = 
   std::memset(&tk, 0, sizeof(tk));
   std::memset(&tv, 0, sizeof(tv));
   bool tma = (p.PS % kTileTok) == 0;
-  if (kv_fp8) {
-    if (D != 128) return fail(MXFA_ERR_UNSUPPORTED, "FP8 caches need head dim 128 (got %d)", D);
-    int swap = 0;
-    if (tma) tma = encode_kv_map_fp8(&tk, p.k, p.v, p.HKV, static_cast<long long>(p.P) * p.PS, &swap);
-    p.kv_swap = tma ? swap : 0;
-    return bf16 ? launch_decode_fp8<__nv_bfloat16>(p, nt, tma, grid, tk, tv, st)
-                : launch_decode_fp8<__half>(p, nt, tma, grid, tk, tv, st);
+  const long long slots = static_cast<long long>(p.P) * p.PS;
+  KvMaps maps;
+  if (tma && !kv_map_cache_get(p.k, p.v, D, p.HKV, slots, kv_fp8, &maps)) {
+    maps = KvMaps{};
+    if (kv_fp8) {
+      maps.tma = D == 128 && encode_kv_map_fp8(&maps.tk, p.k, p.v, p.HKV, slots, &maps.swap);
+    } else if (encode_kv_map_5d(&maps.tk, p.k, p.v, D, p.HKV, slots, &maps.swap)) {
+      // fewest copies per tile that the driver accepts: K+V in one box, else
+      // one box per cache, else one per 64-column block
+      maps.kind = 5;
+      maps.tma = true;
+    } else if (encode_kv_map_4d(&maps.tk, p.k, D, p.HKV, slots) && encode_kv_map_4d(&maps.tv, p.v, D, p.HKV, slots)) {
+      maps.kind = 4;
+      maps.tma = true;
+    } else {
+      maps.kind = 3;
+      maps.tma = encode_kv_map(&maps.tk, p.k, D, p.HKV, slots) && encode_kv_map(&maps.tv, p.v, D, p.HKV, slots);
+    }
+    kv_map_cache_put(p.k, p.v, D, p.HKV, slots, kv_fp8, maps);
   }
   if (tma) {
-    const long long slots = static_cast<long long>(p.P) * p.PS;
-    // fewest copies per tile that the driver accepts: K+V in one box, else
-    // one box per cache, else one per 64-column block
-    int swap = 0;
-    if (encode_kv_map_5d(&tk, p.k, p.v, D, p.HKV, slots, &swap)) {
-      p.kv_map = 5;
-      p.kv_swap = swap;
-    } else if (encode_kv_map_4d(&tk, p.k, D, p.HKV, slots) && encode_kv_map_4d(&tv, p.v, D, p.HKV, slots)) {
-      p.kv_map = 4;
-    } else {
-      p.kv_map = 3;
-      tma = encode_kv_map(&tk, p.k, D, p.HKV, slots) && encode_kv_map(&tv, p.v, D, p.HKV, slots);
-    }
+    tma = maps.tma;
+    tk = maps.tk;
+    tv = maps.tv;
+    p.kv_map = maps.kind;
+    p.kv_swap = maps.swap;
+  }
+  if (kv_fp8) {
+    if (D != 128) return fail(MXFA_ERR_UNSUPPORTED, "FP8 caches need head dim 128 (got %d)", D);
+    if (!tma) p.kv_swap = 0;
+    return bf16 ? launch_decode_fp8<__nv_bfloat16>(p, nt, tma, grid, tk, tv, st)
+                : launch_decode_fp8<__half>(p, nt, tma, grid, tk, tv, st);
   }
   if (bf16)
     return D == 128 ? launch_decode_t<__nv_bfloat16, 128>(p, nt, tma, grid, tk, tv, st)

@@ -42,12 +42,22 @@ def get_last_dispatch_info() -> DispatchInfo | None:
     return getattr(_state, "dispatch_info", None)
 
 
+_EXTENSION: list[Any] = []  # the imported backend module, once found
+
+
 def _native_extension() -> Any | None:
     """The backend module, or None when it cannot be imported (tests replace this)."""
+    if _EXTENSION:
+        return _EXTENSION[0]
     try:
-        return importlib.import_module(_EXTENSION_MODULE)
+        module = importlib.import_module(_EXTENSION_MODULE)
     except (ImportError, OSError):
         return None
+    _EXTENSION.append(module)
+    return module
+
+
+_INFOS: dict[str, DispatchInfo] = {}  # immutable records, one per operation
 
 
 def native_unavailable_reason(tensor: Any, operation: str) -> str | None:
@@ -83,7 +93,10 @@ def dispatch(operation: str, tensor: Any, extension_args: tuple[Any, ...]) -> An
                 raise
             reason = f"native_call_failed:{exc}"
         else:
-            _state.dispatch_info = DispatchInfo(backend=BACKEND_LABEL, operation=operation)
+            info = _INFOS.get(operation)
+            if info is None:
+                info = _INFOS[operation] = DispatchInfo(backend=BACKEND_LABEL, operation=operation)
+            _state.dispatch_info = info
             return result
     hint = ""
     if os.getenv("MXFLASHATTN_ALLOW_FALLBACK", "").strip() == "1":
