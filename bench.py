@@ -35,7 +35,7 @@ HQ, HKV, D, PS, BATCH, LAYERS = 32, 8, 128, 16, 128, 36
 # DRAM traffic (read + write) of one decode launch of the default workload
 # (batch 128, seed 2026), from the ncu capture in
 # profiles/paged_decode_qwen3_4b_b128.md.
-NCU_TRAFFIC_BYTES = {(128, 2026): 378.800896e6}
+NCU_TRAFFIC_BYTES = {(128, 2026): 381.832192e6}
 METRIC = "decode-attn KV HBM GB/s & tok/s (Qwen3-4B shape, b128) at 1/2/4/8 B200"
 WORKLOAD = "qwen3-4b paged decode attention, b128, 36 layers (config 2)"
 
