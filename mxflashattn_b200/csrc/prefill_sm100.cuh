@@ -202,59 +202,6 @@ struct TcBars {
   uint64_t s_full[2], p_full[2], pv_done[2];
 };
 
-// ------------------------------------------------- softmax arithmetic off XU
-//
-// The softmax warps are bound by the XU pipe (MUFU ex2 and the f32 -> bf16x2
-// conversion both run there, at a fraction of the FMA/ALU rate).  Two
-// substitutions move work to the other pipes without changing the math:
-//
-// exp2_fma: 2^x on the FMA pipe for a share of the elements.  x is split into
-//   n = round(x) (a 1.5*2^23 add leaves n in the low mantissa bits) and
-//   f = x - n in [-0.5, 0.5]; 2^f is a degree-4 polynomial (coefficients from
-//   a relative-error least-squares fit on [-0.5, 0.5], max error 2.7e-6 in
-//   float), and 2^n is added to the exponent field with one integer add.
-//   x <= -126 (including -inf for masked keys) gives exactly 0.
-// pack_bf16_rne: two non-negative finite floats to bf16x2 with round to
-//   nearest even done by integer adds (bit-identical to cvt.rn.bf16x2.f32).
-#ifndef MXFA_PF_POLY_MASK
-#define MXFA_PF_POLY_MASK 0x88  // element e of a row uses exp2_fma when bit (e & 7) is set
-#endif
-
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -126.f);
-  const float t = xc + 12582912.f;  // 1.5 * 2^23
-  const float n = t - 12582912.f;
-  const float f = xc - n;
-  float q = 0.009570610709488392f;
-  q = fmaf(q, f, 0.055917903780937195f);
-  q = fmaf(q, f, 0.24024732410907745f);
-  q = fmaf(q, f, 0.6931217908859253f);
-  q = fmaf(q, f, 0.9999992847442627f);
-  const float r = __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-  return x > -126.f ? r : 0.f;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16_rne(float a, float b) {
-  uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
-  ua += 0x7FFFu + ((ua >> 16) & 1u);
-  ub += 0x7FFFu + ((ub >> 16) & 1u);
-  return __byte_perm(ua, ub, 0x7632);
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack_p(float a, float b) {
-  if constexpr (std::is_same_v<T, __nv_bfloat16>)
-    return pack_bf16_rne(a, b);
-  else
-    return Elem<T>::pack(a, b);
-}
-
-// Element e of a row: 2^x on MUFU or on the FMA pipe (the choice folds to a
-// constant once the row loop is unrolled).
-__device__ __forceinline__ float softmax_exp2(float x, int e) {
-  return ((MXFA_PF_POLY_MASK >> (e & 7)) & 1) ? exp2_fma(x) : fast_exp2(x);
-}
-
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
