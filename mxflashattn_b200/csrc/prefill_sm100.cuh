@@ -90,6 +90,71 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// A chain of MMAs into one accumulator, issued from one asm block: descriptors
+// (and tensor-memory A addresses) are computed by the caller ahead of time,
+// so issuing is back-to-back tcgen05.mma instructions.  The first MMA of an
+// SS chain starts the accumulator; a TS chain's first MMA accumulates when
+// `acc` is non-zero; every later MMA accumulates.
+__device__ __forceinline__ void umma_ss_chain(uint32_t d, const uint64_t (&a)[8], const uint64_t (&b)[8],
+                                              uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred pf, pt;\n\t"
+      "setp.ne.b32 pf, %17, %17;\n\tsetp.eq.b32 pt, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %9, %17, pf;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %10, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %11, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %12, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %13, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %14, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %15, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %16, %17, pt;\n\t}" ::"r"(d),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(b[0]),
+      "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ss_chain(uint32_t d, const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                              uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred pf, pt;\n\t"
+      "setp.ne.b32 pf, %9, %9;\n\tsetp.eq.b32 pt, %9, %9;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, pf;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, pt;\n\t}" ::"r"(d),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_chain(uint32_t d, const uint32_t (&a)[8], const uint64_t (&b)[8],
+                                              uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred pa, pt;\n\t"
+      "setp.ne.b32 pa, %18, 0;\n\tsetp.eq.b32 pt, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %17, pa;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %13, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %14, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %15, %17, pt;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %16, %17, pt;\n\t}" ::"r"(d),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "l"(b[0]),
+      "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Make values opaque to the compiler at this point, so they are computed
+// here (ahead of a wait) and not re-derived next to their use.
+template <int N>
+__device__ __forceinline__ void pin_regs(uint64_t (&x)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+l"(x[i]));
+}
+template <int N>
+__device__ __forceinline__ void pin_regs(uint32_t (&x)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(x[i]));
+}
+
 #define MXFA_R32(x)                                                                                             \
   "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]), "=r"(x[8]),   \
       "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15]), "=r"(x[16]),    \
@@ -324,42 +389,75 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc<T>(kTcRows, kTcKeys, false);
       constexpr uint32_t idesc_o = umma_idesc<T>(kTcRows, HD, true);
-      const uint32_t q_base = smem_u32(sm + Cfg::kQ);
-      auto issue_s = [&](int t) -> bool {
-        const int sb = t & 1, st = t % NS;
-        if (!tc_wait(&bars->k_full[st], (t / NS) & 1, abort)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sm + Cfg::kK + st * Cfg::kTile);
+      constexpr int kS = HD / 16;        // K-steps of a score product
+      constexpr int kP = kTcKeys / 16;   // K-steps of a P.V product
+      // Descriptor start addresses are in 16-byte units (bits 0-13) and every
+      // operand lies inside shared memory, so a step is a plain add.  Q and K
+      // (K-major) advance 32 bytes per 16-column step within a 128-byte row
+      // and a whole 64-column block every four steps; V (MN-major) advances 16
+      // key rows = 2 KB per step.
+      auto s_step = [](int kk) -> uint64_t { return (kk >> 2) * (Cfg::kBlk >> 4) + (kk & 3) * 2; };
+      uint64_t qd[kS];
+      {
+        const uint64_t base = smem_desc(smem_u32(sm + Cfg::kQ), 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Cfg::kBlk + (kk & 3) * 32;
-          umma_f16(tmem + sb * kTcKeys, smem_desc(q_base + off, 16, 1024), smem_desc(k_base + off, 16, 1024),
-                   idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars->s_full[sb]);
-        umma_commit(&bars->k_empty[st]);
-        return true;
+        for (int kk = 0; kk < kS; ++kk) qd[kk] = base + s_step(kk);
+      }
+      auto k_descs = [&](int st, uint64_t (&kd)[kS]) {
+        const uint64_t base = smem_desc(smem_u32(sm + Cfg::kK + st * Cfg::kTile), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kS; ++kk) kd[kk] = base + s_step(kk);
       };
       bool ok = tc_wait(&bars->q_full, 0, abort);
-      if (ok) ok = issue_s(0);
-      if (ok && nkt > 1) ok = issue_s(1);
-      for (int j = 0; j < nkt && ok; ++j) {
-        const int pb = j & 1, vs = j % NS;
-        if (!tc_wait(&bars->p_full[pb], (j >> 1) & 1, abort)) break;
-        if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
+      for (int t = 0; t < 2 && t < nkt && ok; ++t) {
+        uint64_t kd[kS];
+        k_descs(t % NS, kd);
+        const int st = t % NS;
+        if (!tc_wait(&bars->k_full[st], (t / NS) & 1, abort)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t v_base = smem_u32(sm + Cfg::kV + vs * Cfg::kTile);
+        umma_ss_chain(tmem + t * kTcKeys, qd, kd, idesc_s);
+        umma_commit(&bars->s_full[t]);
+        umma_commit(&bars->k_empty[st]);
+      }
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int pb = j & 1, vs = j % NS, ks = (j + 2) % NS;
+        const bool next_s = j + 2 < nkt;
+        // everything the two products need is computed before the waits
+        uint64_t vd[kP], kd[kS];
+        uint32_t pa[kP];
+        {
+          const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
 #pragma unroll
-        for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-          const uint64_t vd = smem_desc(v_base + kk * 16 * 128, Cfg::kBlk, 1024);
-          // 16 keys = 8 packed columns of P_j (written over S_j in buffer j%2)
-          umma_f16_ts(tmem + Cfg::kTmemO + pb * HD, tmem + pb * kTcKeys + kk * 8, vd, idesc_o,
-                      (j >= 2 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kP; ++kk) {
+            vd[kk] = vbase + kk * (16 * 128 >> 4);
+            // 16 keys = 8 packed columns of P_j (written over S_j in buffer j%2)
+            pa[kk] = tmem + pb * kTcKeys + kk * 8;
+          }
+        }
+        k_descs(ks, kd);
+        pin_regs(vd);
+        pin_regs(kd);
+        pin_regs(pa);
+        // K_{j+2} and V_j landed long before P_j is ready: wait for them
+        // first, so nothing but P_j stands between the softmax and the two
+        // products
+        if (next_s && !tc_wait(&bars->k_full[ks], ((j + 2) / NS) & 1, abort)) break;
+        if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
+        if (!tc_wait(&bars->p_full[pb], (j >> 1) & 1, abort)) break;
+        tc_fence_after();
+        umma_ts_chain(tmem + Cfg::kTmemO + pb * HD, pa, vd, idesc_o, j >= 2 ? 1u : 0u);
+        // S_{j+2} reuses buffer j%2; it is issued after the P.V product above
+        if (next_s) umma_ss_chain(tmem + pb * kTcKeys, qd, kd, idesc_s);
+        // each commit tracks every product issued before it
+        if (next_s) {
+          umma_commit(&bars->s_full[pb]);
+          umma_commit(&bars->k_empty[ks]);
         }
         umma_commit(&bars->pv_done[pb]);
         umma_commit(&bars->v_empty[vs]);
-        // S_{j+2} reuses buffer j%2; it is issued after the P.V product above
-        if (j + 2 < nkt && !issue_s(j + 2)) break;
       }
     }
     __syncwarp();
