@@ -546,6 +546,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
   // Q^T fragments (B operand): thread holds Q[row g][d = kk*16 + 2*t4 + {0,1}, +8]
   uint32_t qf[HD / 16][NT][2];
   int lim[NT][2];  // last visible key position of the two rows this thread owns in each n-tile
+  int lim_min = 0x7fffffff;  // the smallest of them over rows that exist
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int row = row_base + nt * 8 + g;
@@ -579,6 +580,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
         lim[nt][c] = total_len - p.Sq + col_row / p.GQ;
       else
         lim[nt][c] = 0x7fffffff;
+      if (col_row < rows_total) lim_min = min(lim_min, lim[nt][c]);
     }
   }
 
@@ -620,6 +622,10 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
     if constexpr (kFp8) {
+      // odd K-steps accumulate separately: two independent MMA chains
+      float s2[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) s2[nt][0] = s2[nt][1] = s2[nt][2] = s2[nt][3] = 0.f;
       // one ldmatrix.x4 = two 16-column steps x two 8-token halves of fp8 K;
       // each register (4 e4m3 values) becomes the step's low and high f16x2
       const int q8 = lane >> 3;
@@ -635,9 +641,14 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
           e4m3x4_to_f16x2x2(x[2 * h], lo0, hi0);
           e4m3x4_to_f16x2x2(x[2 * h + 1], lo1, hi1);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Elem<MT>::mma(s[nt], lo0, lo1, hi0, hi1, qf[kk][nt][0], qf[kk][nt][1]);
+          for (int nt = 0; nt < NT; ++nt)
+            Elem<MT>::mma(h ? s2[nt] : s[nt], lo0, lo1, hi0, hi1, qf[kk][nt][0], qf[kk][nt][1]);
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
     } else {
       const int q8 = lane >> 3;
       const int r = ((q8 & 1) << 3) + (lane & 7);
@@ -651,15 +662,24 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
       }
     }
 
-    // mask + scale into the log2 domain
+    // mask + scale into the log2 domain.  On the e4m3 path (instruction
+    // bound), a tile inside [lo, hi) whose last key every existing row sees
+    // needs no mask (rows past rows_total have q = 0 and are never read back).
+    if (kFp8 && !partial && pos0 + kTileTok - 1 <= lim_min) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int pos = pos0 + g + ((e >> 1) << 3);
-        const bool ok = pos >= lo && pos < hi && pos <= lim[nt][e & 1];
-        s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
-      }
+        for (int e = 0; e < 4; ++e) s[nt][e] *= p.scale_log2;
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int pos = pos0 + g + ((e >> 1) << 3);
+          const bool ok = pos >= lo && pos < hi && pos <= lim[nt][e & 1];
+          s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
+        }
+    }
 
     // online softmax per query row (a column of S^T)
     float alpha[NT][2];
