@@ -692,7 +692,11 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float m_new = fmaxf(m[nt][c], mx);
+        // the e4m3 path keeps its running max until a tile's max exceeds it
+        // by more than 2^8 (P then stays below 256, exact in f16 with the
+        // hi/lo split), which skips most O rescales
+        const float m_cand = fmaxf(m[nt][c], mx);
+        const float m_new = (kFp8 && m_cand <= m[nt][c] + 8.f) ? m[nt][c] : m_cand;
         float a = 1.f, p0 = 0.f, p1 = 0.f;
         if (m_new != -INFINITY) {
           a = fast_exp2(m[nt][c] - m_new);
