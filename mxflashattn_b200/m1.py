@@ -21,6 +21,11 @@ from . import _lib
 def paged_decode_split(q, k, v, bt, sl, scale, stream, np, c_len):
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise RuntimeError("tensors must be on device")
+    # Stricter than the reference binding, which checks q/k/v only: a block
+    # table, lengths or cache on another device would reach the kernel as a
+    # foreign pointer, so they are rejected with the same message instead.
+    if any(t.device != q.device for t in (k, v, bt, sl)):
+        raise RuntimeError("tensors must be on device")
     ok = (q.dtype in (torch.float16, torch.bfloat16) and q.dtype == k.dtype == v.dtype and q.is_contiguous()
           and k.is_contiguous() and v.is_contiguous() and bt.is_contiguous() and sl.is_contiguous()
           and sl.dtype == torch.int32 and bt.dtype == torch.int32)

@@ -196,6 +196,13 @@ def test_reference_compatible_split_entry_rejects_like_reference(cuda_device):
     with pytest.raises(RuntimeError, match="dtype/layout"):
         m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"].long(), t["cache_seqlens"],
                               0.1, 0, 2, 16)
+    # a host-side block table or length vector is refused before any launch
+    with pytest.raises(RuntimeError, match="on device"):
+        m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"].cpu(), t["cache_seqlens"],
+                              0.1, 0, 2, 16)
+    with pytest.raises(RuntimeError, match="on device"):
+        m1.paged_decode_split(t["q"], t["k_cache"], t["v_cache"], t["block_table"], t["cache_seqlens"].cpu(),
+                              0.1, 0, 2, 16)
 
 
 def test_qwen3_4b_batch128_sampled_against_oracle(cuda_device):
