@@ -189,6 +189,8 @@ class FusedContextParallelDecode:
         from . import _lib, backend
 
         B, Sq, HQ, D = q.shape
+        if any(t.device != self.device for t in (q, k_cache, v_cache, local_seqlens, local_block_table)):
+            raise ValueError(f"every tensor must be on {self.device}, the device this exchange was built on")
         if (B, HQ, k_cache.shape[2], D) != self.geometry or Sq != 1:
             raise ValueError(f"call geometry {(B, HQ, k_cache.shape[2], D)} (Sq={Sq}) does not match "
                              f"{self.geometry} with one query token")
