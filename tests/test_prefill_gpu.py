@@ -152,3 +152,64 @@ def test_no_reads_past_the_packed_tensors(causal, cuda_device):
     assert_close_out(host(out), ref, "bf16", f"poisoned tail causal={causal}",
                      extra=p_rounding_bound("bf16", oracle.attention_varlen(
                          case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, causal=causal)))
+
+
+def _rescale_case(seed, lens, dt, boost_every=197, boost=12.0):
+    """Varlen q/k/v ~ N(0,1) whose keys at every ``boost_every``-th position are scaled by ``boost``.
+
+    Those keys' scores sit far above everything before them, so row maxima
+    jump past the lazy-rescale threshold deep into each sequence, after both
+    softmax groups' first tiles: the accumulators are rescaled in tensor
+    memory mid-sequence.  A stride of 197 puts the boosted keys in key tiles
+    1, 3, 4, 6 and 7 of 128, so both softmax groups (odd and even tiles) see
+    jumps after their first tile.
+    """
+    rng = np.random.default_rng(seed)
+    total = sum(lens)
+    q = syn.round_dtype(rng.standard_normal((total, 8, 128), dtype=np.float32), dt)
+    k = rng.standard_normal((total, 2, 128), dtype=np.float32)
+    v = syn.round_dtype(rng.standard_normal((total, 2, 128), dtype=np.float32), dt)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    for s in range(len(lens)):
+        for pos in range(boost_every, lens[s], boost_every):
+            k[cu[s] + pos] *= boost
+    return q, syn.round_dtype(k, dt), v, cu
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+def test_row_max_jumps_rescale_the_accumulators(causal, dt, cuda_device):
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    lens = [1100, 700]
+    q, k, v, cu = _rescale_case(91 + causal, lens, dt)
+    tdt = syn.torch_dtype(dt)
+    tq, tk, tv = (torch.from_numpy(x).to(cuda_device, tdt) for x in (q, k, v))
+    tcu = torch.from_numpy(cu).to(cuda_device)
+    out, lse = backend.flash_attn_varlen_func(tq, tk, tv, tcu, tcu, max(lens), max(lens), causal, 128 ** -0.5,
+                                              return_lse=True)
+    torch.cuda.synchronize()
+    ref, ref_lse = oracle.attention_varlen(q, k, v, cu, cu, causal=causal, return_lse=True)
+    abs_v = oracle.attention_varlen(q, k, np.abs(v), cu, cu, causal=causal)
+    assert_close_out(host(out), ref, dt, f"rescale causal={causal}", extra=p_rounding_bound(dt, abs_v))
+    assert_close_lse(host(lse), ref_lse.T, f"rescale lse causal={causal}")
+
+
+def test_negative_scale_takes_the_row_minimum(cuda_device):
+    """A negative softmax scale: the stable exponent is the row's minimum raw score."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_varlen_func
+
+    lens = [300, 45]
+    case = syn.varlen_case(93, q_lens=lens, q_heads=8, kv_heads=2, head_dim=128, dtype="bf16", causal=True)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    scale = -0.09
+    out = flash_attn_varlen_func(q, k, v, cu_q, cu_k, max(lens), max(lens), softmax_scale=scale, causal=True)
+    torch.cuda.synchronize()
+    ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, softmax_scale=scale, causal=True)
+    abs_v = oracle.attention_varlen(case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, softmax_scale=scale,
+                                    causal=True)
+    assert_close_out(host(out), ref, "bf16", "negative scale", extra=p_rounding_bound("bf16", abs_v))
