@@ -80,7 +80,9 @@ def assert_close_lse(actual, expected, what=""):
     a = np.asarray(actual, np.float64)
     e = np.asarray(expected, np.float64)
     both_inf = np.isneginf(a) & np.isneginf(e)
-    err = float(np.max(np.abs(np.where(both_inf, 0.0, a - e)))) if a.size else 0.0
+    with np.errstate(invalid="ignore"):  # -inf - -inf is masked out just below
+        diff = a - e
+    err = float(np.max(np.abs(np.where(both_inf, 0.0, diff)))) if a.size else 0.0
     assert err <= LSE_ATOL, f"{what}: LSE max abs err {err:.3e} > {LSE_ATOL:.0e}"
 
 

@@ -140,3 +140,32 @@ def test_fp8_single_launch_equals_two_launches(cuda_device):
             for s in (False, True)]
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("splits", [0, 3])
+def test_fp8_row_max_jumps_rescale(splits, cuda_device):
+    """Keys scaled x12 at every 37th position: row maxima jump past the e4m3 path's 2^8 rescale threshold
+    on many tiles after the first, so the accumulators are rescaled mid-sequence (and across splits)."""
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    case = syn.paged_case(1480 + splits, batch=3, q_heads=16, kv_heads=4, head_dim=128, dtype="bf16", page_size=16,
+                          lengths=[900, 333, 1200])
+    k_cache = case.k_cache.copy()
+    for b, L in enumerate(case.cache_seqlens):
+        for pos in range(5, int(L), 37):
+            k_cache[case.block_table[b, pos // 16], pos % 16] *= 12.0
+    case = dataclasses.replace(case, k_cache=k_cache)
+    k_scale, v_scale = 0.25, 1.0  # boosted keys stay below e4m3's 448 after dividing by k_scale
+    fp8, deq = _fp8_case(case, k_scale, v_scale)
+    t = _dev(case, fp8, cuda_device)
+    cap = 16 * case.block_table.shape[1]
+    chunk = -(-cap // splits) if splits else 0
+    out, lse = backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                         case.softmax_scale, False, return_lse=True, num_splits=splits,
+                                         chunk_len=chunk, k_scale=k_scale, v_scale=v_scale)
+    torch.cuda.synchronize()
+    ref, ref_lse = oracle_paged(deq)[:2]
+    assert_close_out(host(out), ref, "bf16", f"fp8 rescale splits{splits}")
+    assert_close_lse(host(lse), ref_lse, f"fp8 rescale lse splits{splits}")
