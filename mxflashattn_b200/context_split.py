@@ -1,6 +1,6 @@
 """Decode across GPUs: batch / KV-head sharding and long-context splitting.
 
-Two partitionings of the decode path, one process per GPU:
+Partitionings of the attention path, one process per GPU:
 
 * **Batch or KV-head groups** (``shard_batch`` / ``shard_kv_heads``): every
   (sequence, KV head) unit is independent, so each rank decodes its share
@@ -12,6 +12,9 @@ Two partitionings of the decode path, one process per GPU:
   with ONE all-gather of ``[rows, D + 1]`` fp32 per layer, and every rank
   merges them locally with ``mxfa_lse_merge_launch``.  Only those small
   records cross NVLink; KV pages never leave the GPU that owns them.
+* **Prefill by KV-head groups** (``prefill_local_heads``): each rank runs the
+  varlen forward over its KV heads and the query heads that read them; heads
+  are independent, so there is no communication.
 
 The reference runs on one device only; this module is new.  The exchange
 (``gather_partials``) is a plain ``torch.distributed`` collective, so the
@@ -38,6 +41,32 @@ def shard_kv_heads(kv_heads: int, world_size: int, rank: int) -> range:
         raise ValueError(f"{kv_heads} KV heads do not divide over {world_size} ranks")
     per = kv_heads // world_size
     return range(rank * per, (rank + 1) * per)
+
+
+def prefill_local_heads(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, *, world_size: int,
+                        rank: int, causal: bool = True, softmax_scale=None, return_lse: bool = False):
+    """This rank's share of a varlen prefill: KV heads ``shard_kv_heads(HKV, world, rank)``.
+
+    ``q`` is ``[Tq, HQ, D]`` and ``k``/``v`` are ``[Tk, HKV, D]`` with every head.
+    The output (and LSE) cover query heads ``[hk0*GQ, hk1*GQ)`` only, where
+    GQ = HQ / HKV, because query head h reads KV head h // GQ.  Concatenating
+    the ranks' outputs along the head axis gives the full result bit for
+    bit.  A tensor-parallel model that already holds only its own heads calls
+    ``backend.flash_attn_varlen_func`` on them directly.
+    """
+    from . import backend
+
+    hq, hkv, d = q.shape[1], k.shape[1], q.shape[2]
+    if hq % hkv:
+        raise ValueError(f"{hq} query heads are not a multiple of {hkv} KV heads")
+    heads = shard_kv_heads(hkv, world_size, rank)
+    gq = hq // hkv
+    qs = q[:, heads.start * gq:heads.stop * gq].contiguous()
+    ks = k[:, heads.start:heads.stop].contiguous()
+    vs = v[:, heads.start:heads.stop].contiguous()
+    scale = softmax_scale if softmax_scale is not None else d ** -0.5
+    return backend.flash_attn_varlen_func(qs, ks, vs, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                                          causal, scale, return_lse=return_lse)
 
 
 def shard_ranges(lengths, world_size: int, page_size: int) -> np.ndarray:

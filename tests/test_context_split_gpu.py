@@ -221,3 +221,25 @@ def test_exchange_wait_times_out_and_reports(cuda_device):
         assert float((x * 2).sum()) == 8.0
     finally:
         _lib.check(lib.mxfa_peer_free(buf), "mxfa_peer_free")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_prefill_kv_head_shards_reassemble_the_full_result(world, cuda_device):
+    """Emulated ranks on one device: each rank's KV-head share, concatenated over heads, equals the whole call."""
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    lens = [700, 129, 1]
+    case = syn.varlen_case(310 + world, q_lens=lens, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16",
+                           causal=True)
+    tdt = syn.torch_dtype(case.dtype)
+    q, k, v = (torch.from_numpy(x).to(cuda_device, tdt) for x in (case.q, case.k, case.v))
+    cu = torch.from_numpy(case.cu_q).to(cuda_device)
+    full, full_lse = backend.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True,
+                                                    case.softmax_scale, return_lse=True)
+    parts = [cs.prefill_local_heads(q, k, v, cu, cu, max(lens), max(lens), world_size=world, rank=r, causal=True,
+                                    softmax_scale=case.softmax_scale, return_lse=True) for r in range(world)]
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat([o for o, _ in parts], dim=1), full)
+    assert torch.equal(torch.cat([lse for _, lse in parts], dim=1), full_lse)
