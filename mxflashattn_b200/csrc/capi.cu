@@ -889,7 +889,7 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
   if (!encode_rows_map(&mq, q, D, HQ, total_q, kTcRows) || !encode_rows_map(&mk, k, D, HKV, total_k, kTcKeys) ||
       !encode_rows_map(&mv, v, D, HKV, total_k, kTcKeys))
     return fail(MXFA_ERR_UNSUPPORTED, "TMA descriptor encoding failed for the prefill operands");
-  dim3 grid((max_q + kTcRows - 1) / kTcRows, HQ, B);
+  dim3 grid(HQ, B, (max_q + kTcRows - 1) / kTcRows);
   auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;
     kern<<<grid, kTcThreads, smem, st>>>(p, mq, mk, mv);

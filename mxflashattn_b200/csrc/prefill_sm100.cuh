@@ -296,8 +296,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kBar + Cfg::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int b = blockIdx.z;
-  const int h = blockIdx.y;
+  // Grid: x = query head, y = sequence, z = query tile (slowest).  Blocks go
+  // out in linear order, so every head and sequence's latest (heaviest, for
+  // causal) tiles start before any lighter tile: heaviest first across the
+  // whole grid, which leaves only light tiles for the tail.
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
   const int hk = h / p.GQ;
   int q_start, q_len, k_start, k_len;
   if (p.cu_q != nullptr) {
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     k_start = b * p.Sk;
     k_len = p.Sk;
   }
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest, causal) tiles first
+  const int qt = gridDim.z - 1 - blockIdx.z;
   const int q0 = qt * kTcRows;
   if (q0 >= q_len) return;
   const int shift = k_len - q_len;
