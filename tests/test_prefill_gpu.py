@@ -213,3 +213,23 @@ def test_negative_scale_takes_the_row_minimum(cuda_device):
     abs_v = oracle.attention_varlen(case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, softmax_scale=scale,
                                     causal=True)
     assert_close_out(host(out), ref, "bf16", "negative scale", extra=p_rounding_bound("bf16", abs_v))
+
+
+def test_many_sequences_with_keys_longer_than_queries(cuda_device):
+    """200 sequences, q 1-260 tokens, k = q + 0-400 tokens (chunked-prefill shape): bottom-right causal
+    masking across several tiles, a grid that is mostly empty query tiles, every row checked."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_varlen_func
+
+    rng = np.random.default_rng(2024)
+    q_lens = rng.integers(1, 261, size=200).tolist()
+    k_lens = [q + int(rng.integers(0, 401)) for q in q_lens]
+    case = syn.varlen_case(2024, q_lens=q_lens, k_lens=k_lens, q_heads=8, kv_heads=2, head_dim=128, dtype="bf16",
+                           causal=True)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out = flash_attn_varlen_func(q, k, v, cu_q, cu_k, max(q_lens), max(k_lens), causal=True)
+    torch.cuda.synchronize()
+    ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, causal=True)
+    abs_v = oracle.attention_varlen(case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, causal=True)
+    assert_close_out(host(out), ref, "bf16", "many sequences, k longer than q", extra=p_rounding_bound("bf16", abs_v))
