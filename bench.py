@@ -336,21 +336,27 @@ def run_ours(args):
         out_host = [torch.empty_like(q, pin_memory=True) for q in q_host]
         sl_host = layers[0]["cache_seqlens"].cpu().pin_memory()
         q_dev = [torch.empty_like(t["q"]) for t in layers]
-        sl_dev = torch.empty_like(layers[0]["cache_seqlens"])
+        # lengths alternate between two device buffers by step parity, so a
+        # step's upload never waits for the previous step's last layer
+        sl_dev = [torch.empty_like(layers[0]["cache_seqlens"]) for _ in range(2)]
         h2d = torch.cuda.Stream(device)
         d2h = torch.cuda.Stream(device)
         ev_in = [torch.cuda.Event() for _ in layers]
         ev_done = [torch.cuda.Event() for _ in layers]
         ev_sl = torch.cuda.Event()
+        ev_step = [torch.cuda.Event() for _ in range(2)]
+        parity = [0]
 
         def e2e_step_tables():
             # Copies run on their own streams so layer i+1's upload and layer i's
-            # read-back overlap layer i's kernel; every copy stays inside the
+            # read-back overlap layer i's kernel, and a step's uploads overlap
+            # the previous step's last layers; every copy stays inside the
             # timed region.  q buffers are reused only after the previous
             # step's kernel that read them has finished.
+            sl = sl_dev[parity[0]]
             with torch.cuda.stream(h2d):
-                h2d.wait_event(ev_done[-1])  # every layer of the previous step has read sl_dev
-                sl_dev.copy_(sl_host, non_blocking=True)
+                h2d.wait_event(ev_step[parity[0]])  # the step two back has finished reading this buffer
+                sl.copy_(sl_host, non_blocking=True)
                 ev_sl.record(h2d)
                 for i in range(len(layers)):
                     h2d.wait_event(ev_done[i])
@@ -359,14 +365,16 @@ def run_ours(args):
             stream.wait_event(ev_sl)
             for i, t in enumerate(layers):
                 stream.wait_event(ev_in[i])
-                o = flash_attn_with_kvcache(q_dev[i], t["k_cache"], t["v_cache"], cache_seqlens=sl_dev,
+                o = flash_attn_with_kvcache(q_dev[i], t["k_cache"], t["v_cache"], cache_seqlens=sl,
                                             block_table=t["block_table"], softmax_scale=scale)
                 ev_done[i].record(stream)
                 o.record_stream(d2h)
                 with torch.cuda.stream(d2h):
                     d2h.wait_event(ev_done[i])
                     out_host[i].copy_(o, non_blocking=True)
-            stream.wait_stream(d2h)
+            ev_step[parity[0]].record(stream)
+            parity[0] ^= 1
+            stream.wait_stream(d2h)  # bounds the read-back backlog (outputs are freed as their copies finish)
 
         for _ in range(3):
             e2e_step_tables()
@@ -388,7 +396,7 @@ def run_ours(args):
         e_step = e_ms / args.steps
         q_bytes = sum(q.numel() * q.element_size() for q in q_host)
         e2e = {"value": world * bytes_step / (e_step * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": q_bytes + sl_host.numel() * 4,
+               "h2d_bytes_per_step": q_bytes + sl_host.numel() * sl_host.element_size(),
                "d2h_bytes_per_step": sum(o.numel() * o.element_size() for o in out_host),
                "ms_per_step": e_step, "tok_per_s": world * args.batch / (e_step * 1e-3)}
 
