@@ -163,60 +163,133 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
+// Rows of one split's partial output, loaded as this lane's HD/32 columns.
+template <int HD>
+__device__ __forceinline__ void load_partial(const float* src, float (&o)[HD / 32]) {
+  if constexpr (HD / 32 == 4) {
+    const float4 o4 = __ldcg(reinterpret_cast<const float4*>(src));
+    o[0] = o4.x; o[1] = o4.y; o[2] = o4.z; o[3] = o4.w;
+  } else {
+    const float2 o2 = __ldcg(reinterpret_cast<const float2*>(src));
+    o[0] = o2.x; o[1] = o2.y;
+  }
+}
+
+// The reduction behind merge_split_row and merge_split_row_publish: M, L and
+// the unnormalised sum of the weighted partial rows (this lane's columns).
+// For NP <= 64 every lane loads the (m, d) pairs of splits lane and lane+32
+// once, in the same round as the first 8 partial rows; the weights reach the
+// other lanes by shuffle (-1 marks a split with nothing to add), and the
+// remaining partial rows follow 8 at a time.  A merge is then ceil(NP/8)
+// dependent L2 round trips instead of two more for the two passes over the
+// pairs.  The arithmetic and its order are those of the loop form below
+// (used for NP > 64, and always when kChunked is false): the same M, L and
+// accumulation, bit for bit.
+template <int HD, bool kChunked = true>
+__device__ __forceinline__ void merge_split_core(const float* ows, const float* mdws, int r, int NP, int lane,
+                                                 float (&acc)[HD / 32], float& M_out, float& L_out) {
+  constexpr int kPer = HD / 32;
+  constexpr int kChunk = 8;
+  const float2* md = reinterpret_cast<const float2*>(mdws + static_cast<size_t>(r) * NP * 2);
+  const float* src = ows + static_cast<size_t>(r) * NP * HD + lane * kPer;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  float M = -INFINITY, L = 0.f;
+  if (kChunked && NP <= 64) {
+    float2 v0 = make_float2(-INFINITY, 0.f), v1 = make_float2(-INFINITY, 0.f);
+    if (lane < NP) v0 = __ldcg(md + lane);
+    if (lane + 32 < NP) v1 = __ldcg(md + lane + 32);
+    float o[kChunk][kPer];
+#pragma unroll
+    for (int c = 0; c < kChunk; ++c)
+      if (c < NP) load_partial<HD>(src + static_cast<size_t>(c) * HD, o[c]);
+    const bool ok0 = v0.x > -INFINITY && v0.y > 0.f;
+    const bool ok1 = v1.x > -INFINITY && v1.y > 0.f;
+    if (ok0) M = fmaxf(M, v0.x);
+    if (ok1) M = fmaxf(M, v1.x);
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+    float w0 = -1.f, w1 = -1.f;
+    if (M != -INFINITY) {
+      if (ok0) {
+        w0 = fast_exp2(v0.x - M);
+        L += v0.y * w0;
+      }
+      if (ok1) {
+        w1 = fast_exp2(v1.x - M);
+        L += v1.y * w1;
+      }
+    }
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+    if (M != -INFINITY) {
+      for (int base = 0; base < NP; base += kChunk) {
+        if (base > 0) {
+#pragma unroll
+          for (int c = 0; c < kChunk; ++c)
+            if (base + c < NP) load_partial<HD>(src + static_cast<size_t>(base + c) * HD, o[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < kChunk; ++c) {
+          const int pz = base + c;
+          // every lane takes part in both shuffles (pz is warp-uniform)
+          const float wa = __shfl_sync(0xffffffffu, w0, pz & 31);
+          const float wb = __shfl_sync(0xffffffffu, w1, pz & 31);
+          const float w = pz < 32 ? wa : wb;
+          if (pz < NP && w >= 0.f) {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) acc[j] = fmaf(w, o[c][j], acc[j]);
+          }
+        }
+      }
+    }
+  } else {
+    for (int pz = lane; pz < NP; pz += 32) {
+      const float2 v = __ldcg(md + pz);
+      if (v.x > -INFINITY && v.y > 0.f) M = fmaxf(M, v.x);
+    }
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+    if (M != -INFINITY) {
+      for (int pz = lane; pz < NP; pz += 32) {
+        const float2 v = __ldcg(md + pz);
+        if (v.x > -INFINITY && v.y > 0.f) L += v.y * fast_exp2(v.x - M);
+      }
+    }
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+    if (M != -INFINITY) {
+      // loads are unconditional (every split's row is in bounds) so the
+      // unrolled iterations issue them back to back; empty or invalid splits
+      // are dropped by a select, never by multiplying their (unread) values
+#pragma unroll 8
+      for (int pz = 0; pz < NP; ++pz) {
+        const float2 v = __ldcg(md + pz);
+        float o[kPer];
+        load_partial<HD>(src + static_cast<size_t>(pz) * HD, o);
+        const bool valid = v.x > -INFINITY && v.y > 0.f;
+        const float w = fast_exp2(v.x - M);
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) acc[j] = valid ? fmaf(w, o[j], acc[j]) : acc[j];
+      }
+    }
+  }
+  M_out = M;
+  L_out = L;
+}
+
 // Merge the NP split partials of query row r (one warp; lanes own HD/32
 // contiguous columns): M = max m_z, L = sum d_z 2^(m_z - M), O = sum o_z
 // 2^(m_z - M) / L -- the merge algebra of the reference combine
-// (csrc_native/m1_kernel.cpp:862-888), evaluated in two passes so no load
-// waits on the previous split: the lanes first reduce M and L over the
-// splits, then the weighted sum runs with several partial rows in flight.
+// (csrc_native/m1_kernel.cpp:862-888), reduced by merge_split_core.
 // Partials are read past L1 (__ldcg) so a merge may run in the launch that
 // wrote them.
-template <typename T, int HD>
+template <typename T, int HD, bool kChunked = true>
 __device__ __forceinline__ void merge_split_row(const float* ows, const float* mdws, int r, int NP, int lane,
                                                 T* out, float* out_f32, float* lse) {
   constexpr int kPer = HD / 32;
-  const float* md = mdws + static_cast<size_t>(r) * NP * 2;
-  float M = -INFINITY;
-  for (int pz = lane; pz < NP; pz += 32) {
-    const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-    if (v.x > -INFINITY && v.y > 0.f) M = fmaxf(M, v.x);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float L = 0.f;
-  if (M != -INFINITY) {
-    for (int pz = lane; pz < NP; pz += 32) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-      if (v.x > -INFINITY && v.y > 0.f) L += v.y * fast_exp2(v.x - M);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  float acc[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
-  if (M != -INFINITY) {
-    const float* src = ows + static_cast<size_t>(r) * NP * HD + lane * kPer;
-    // loads are unconditional (every split's row is in bounds) so the
-    // unrolled iterations issue them back to back; empty or invalid splits
-    // are dropped by a select, never by multiplying their (unread) values
-#pragma unroll 8
-    for (int pz = 0; pz < NP; ++pz) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-      float o[kPer];
-      if constexpr (kPer == 4) {
-        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(pz) * HD));
-        o[0] = o4.x; o[1] = o4.y; o[2] = o4.z; o[3] = o4.w;
-      } else {
-        const float2 o2 = __ldcg(reinterpret_cast<const float2*>(src + static_cast<size_t>(pz) * HD));
-        o[0] = o2.x; o[1] = o2.y;
-      }
-      const bool valid = v.x > -INFINITY && v.y > 0.f;
-      const float w = fast_exp2(v.x - M);
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) acc[j] = valid ? fmaf(w, o[j], acc[j]) : acc[j];
-    }
-  }
+  float acc[kPer], M, L;
+  merge_split_core<HD, kChunked>(ows, mdws, r, NP, lane, acc, M, L);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   if (out != nullptr) {
     T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
@@ -234,45 +307,13 @@ __device__ __forceinline__ void merge_split_row(const float* ows, const float* m
 // f16x2, exact) and both products run in f16; q is converted to f16 once.
 // merge_split_row for the exchange: the normalised f32 row and its LSE are
 // written to the record slot [cp_rank][r] of every rank's exchange buffer.
-template <int HD>
+template <int HD, bool kChunked = true>
 __device__ __forceinline__ void merge_split_row_publish(const float* ows, const float* mdws, int r, int NP,
                                                         int lane, const unsigned long long* bufs, int world,
                                                         int rank, int rows, size_t rec_off) {
   constexpr int kPer = HD / 32;
-  const float* md = mdws + static_cast<size_t>(r) * NP * 2;
-  float M = -INFINITY;
-  for (int pz = lane; pz < NP; pz += 32) {
-    const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-    if (v.x > -INFINITY && v.y > 0.f) M = fmaxf(M, v.x);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float L = 0.f;
-  if (M != -INFINITY) {
-    for (int pz = lane; pz < NP; pz += 32) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-      if (v.x > -INFINITY && v.y > 0.f) L += v.y * fast_exp2(v.x - M);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  float acc[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
-  if (M != -INFINITY) {
-    const float* src = ows + static_cast<size_t>(r) * NP * HD + lane * kPer;
-#pragma unroll 8
-    for (int pz = 0; pz < NP; ++pz) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(md) + pz);
-      const bool valid = v.x > -INFINITY && v.y > 0.f;
-      const float w = fast_exp2(v.x - M);
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const float o = __ldcg(src + static_cast<size_t>(pz) * HD + j);
-        acc[j] = valid ? fmaf(w, o, acc[j]) : acc[j];
-      }
-    }
-  }
+  float acc[kPer], M, L;
+  merge_split_core<HD, kChunked>(ows, mdws, r, NP, lane, acc, M, L);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const float lse = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
   for (int dst = 0; dst < world; ++dst) {
@@ -281,6 +322,21 @@ __device__ __forceinline__ void merge_split_row_publish(const float* ows, const 
     for (int j = 0; j < kPer; ++j) rec[lane * kPer + j] = acc[j] * inv;
     if (lane == 0) rec[HD] = lse;
   }
+}
+
+// The decode kernel's end-of-unit merges, called out of line: their loads
+// and chunk of partial rows then never add to the register pressure of the
+// kernel's main loop (the standalone combine kernels inline the same code).
+template <typename T, int HD>
+__device__ __noinline__ void merge_split_row_call(const float* ows, const float* mdws, int r, int NP, int lane,
+                                                  T* out, float* lse) {
+  merge_split_row<T, HD>(ows, mdws, r, NP, lane, out, nullptr, lse);
+}
+template <int HD>
+__device__ __noinline__ void merge_split_row_publish_call(const float* ows, const float* mdws, int r, int NP,
+                                                          int lane, const unsigned long long* bufs, int world,
+                                                          int rank, int rows, size_t rec_off) {
+  merge_split_row_publish<HD>(ows, mdws, r, NP, lane, bufs, world, rank, rows, rec_off);
 }
 
 template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
@@ -891,11 +947,19 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
         const int i = rr / p.GQ;
         const int h = kvh * p.GQ + rr % p.GQ;
         const int R = (b * p.Sq + i) * p.HQ + h;
-        if (p.cp_bufs != nullptr)
-          merge_split_row_publish<HD>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank, rows_all,
-                                      lay.records + (epoch & 1u) * lay.record_half);
-        else
-          merge_split_row<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
+        if constexpr (kFp8) {
+          // the e4m3 kernel runs at its register cap: the loop form, inline
+          if (p.cp_bufs != nullptr)
+            merge_split_row_publish<HD, false>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank,
+                                               rows_all, lay.records + (epoch & 1u) * lay.record_half);
+          else
+            merge_split_row<T, HD, false>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
+        } else if (p.cp_bufs != nullptr) {
+          merge_split_row_publish_call<HD>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank, rows_all,
+                                           lay.records + (epoch & 1u) * lay.record_half);
+        } else {
+          merge_split_row_call<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), p.lse);
+        }
       }
       if (p.cp_bufs != nullptr) {
         // every writer's records reach every rank before its flag does
