@@ -121,3 +121,33 @@ def test_counter_bytes_geometry():
     assert lib.mxfa_split_counter_bytes(4, 3, 32, 4) == 4 * 4 * 2 * 4       # 24 rows: two groups of 16
     assert lib.mxfa_split_counter_bytes(0, 1, 32, 8) == 0
     assert np.int64(lib.mxfa_split_counter_bytes(2, 1, 30, 8)) == 0          # HQ not a multiple of HKV
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("splits", [63, 64, 65, 96])
+def test_merge_forms_around_64_splits(dt, splits, cuda_device):
+    """Up to 64 splits the merge loads every (m, d) pair in one round; past 64 it takes the loop form.
+
+    Both sides of the boundary must give the same bits in one launch (merge
+    inside the decode kernel) and in two (separate combine kernel), and match
+    the oracle.
+    """
+    import torch
+
+    from mxflashattn_b200 import _lib
+
+    case = syn.paged_case(1400 + splits + (dt == "bf16"), batch=3, q_heads=16, kv_heads=4, head_dim=128, dtype=dt,
+                          page_size=16, lengths=[3000, 1, 1500])
+    cap = 16 * case.block_table.shape[1]
+    chunk = -(-cap // splits)
+    t = to_device(case, cuda_device)
+    out2, lse2 = _run(t, case, splits, chunk, single=False)
+    out1, lse1 = _run(t, case, splits, chunk, single=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2)
+    assert torch.equal(lse1, lse2)
+    assert _lib.read_error_flags() == 0
+    _counters_zero(cuda_device)
+    ref, ref_lse = oracle_paged(case)[:2]
+    assert_close_out(host(out1), ref, dt, f"{splits} splits")
+    assert_close_lse(host(lse1), ref_lse, f"{splits} splits lse")
