@@ -13,9 +13,26 @@ Prints one JSON line (rank 0).  ``value`` is the whole-job KV HBM throughput
 inputs resident; ``e2e`` is the same metric through the public
 ``flash_attn_with_kvcache`` with q copied from pinned host memory and every
 layer's output read back inside the timed region.  Multi-GPU runs are weak
-scaling: every rank decodes its own batch of 128 sequences, no collective on
-the data path.  ``--impl reference`` times the CPU oracle port (the
-reference's PyTorch-CPU algorithm restated in numpy) on the host cores.
+scaling for the headline: every rank decodes its own batch of 128 sequences,
+no collective on the data path.
+
+Extra keys of the same line (each its own measurement, same timing rules):
+  ``fp8``      the headline workload with e4m3 KV caches (half the bytes);
+  ``prefill``  config 5: causal varlen forward over {15000, 1024, 512, 37},
+               Hq=32, Hk=8, D=128, TFLOP/s against the bf16 tensor peak;
+               ``prefill_heads`` (N>1) the same batch split by KV-head groups;
+  ``longctx``  config 5 decode: 16384-token contexts at B=8 and B=1; with N>1
+               every rank holds a page-aligned range of every sequence and the
+               (O, LSE) records are exchanged once per layer, by the fused
+               NVLink peer-store kernels and by one NCCL all-gather, both
+               checked against a one-GPU decode over the whole context;
+  ``strong``   (N>1) the one config-2 batch of 128 split 128/N per rank.
+
+``--impl reference`` times the reference's own CPU path
+(``mxflashattn.flash_attn_with_kvcache`` with MXFLASHATTN_ALLOW_FALLBACK=1,
+installed from the reference checkout into baseline/_ref) on all host cores;
+when that package is absent it times the numpy oracle port instead and says
+so (``kind: "port"``).
 """
 
 from __future__ import annotations
@@ -32,12 +49,17 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 HQ, HKV, D, PS, BATCH, LAYERS = 32, 8, 128, 16, 128, 36
-# DRAM traffic (read + write) of one decode launch of the default workload
-# (batch 128, seed 2026), from the ncu capture in
-# profiles/paged_decode_qwen3_4b_b128.md.
+LONG_CTX = 16384
+LONG_BATCHES = (8, 1)
+PREFILL_LENS = "15000,1024,512,37"
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one decode
+# launch of the default workload (batch 128, seed 2026), taken once by ncu
+# on one launch of this exact command; reported as a profile value
+# (`traffic_source`), not measured by the run that prints it.
 NCU_TRAFFIC_BYTES = {(128, 2026): 381.832192e6}
 METRIC = "decode-attn KV HBM GB/s & tok/s (Qwen3-4B shape, b128) at 1/2/4/8 B200"
 WORKLOAD = "qwen3-4b paged decode attention, b128, 36 layers (config 2)"
+REF_PACKAGE_DIR = os.path.join(REPO, "baseline", "_ref")
 
 
 def parse_args():
@@ -51,11 +73,13 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
                     help="decode: config 2 (headline); prefill: config 5 varlen causal forward")
-    ap.add_argument("--prefill-lens", default="15000,1024,512,37")
+    ap.add_argument("--prefill-lens", default=PREFILL_LENS)
     ap.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
                     help="decode KV cache type (fp8 = float8_e4m3fn at scale 1; bytes counted at 1 B/element)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="headline decode line only (no fp8 / prefill / longctx / strong keys)")
     return ap.parse_args()
 
 
@@ -66,20 +90,24 @@ def dist_env():
     return world, rank, local
 
 
-def measured_peaks():
+def _peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
-            data = json.load(f)
+            return json.load(f)
+    return None
+
+
+def measured_peaks():
+    data = _peaks()
+    if data is not None:
         return float(data["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
 
 
 def measured_tensor_peak():
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
-    if os.path.exists(path):
-        with open(path) as f:
-            data = json.load(f)
+    data = _peaks()
+    if data is not None:
         return float(data["bf16_tflops"]), "measured bf16_tflops (burst)"
     return 1590.0, "fallback bf16 burst"
 
@@ -93,6 +121,13 @@ def cpu_model() -> str:
     except OSError:
         pass
     return "unknown"
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
 # ------------------------------------------------------------------ clocks
@@ -163,124 +198,188 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm)}
 
 
-# --------------------------------------------------------------- reference
+# ------------------------------------------------------- reference CPU path
 
-def cpu_oracle_sample(lengths, seed, n_seqs, dtype="bf16"):
-    """Host inputs for a bounded CPU sample: n_seqs sequences of one layer."""
-    import numpy as np
+def import_reference():
+    """The reference package installed into baseline/_ref, or None when absent."""
+    if not os.path.isdir(os.path.join(REF_PACKAGE_DIR, "mxflashattn")):
+        return None
+    sys.path.insert(0, REF_PACKAGE_DIR)
+    try:
+        import mxflashattn
+    except Exception:  # noqa: BLE001 -- any import failure means: time the port instead
+        return None
+    finally:
+        sys.path.remove(REF_PACKAGE_DIR)
+    return mxflashattn
 
-    from mxflashattn_b200 import synthetic as syn
 
-    sel = [int(x) for x in lengths[:n_seqs]]
-    case = syn.paged_case(seed, batch=len(sel), q_heads=HQ, kv_heads=HKV, head_dim=D, dtype=dtype, page_size=PS,
-                          lengths=sel)
-    return case, syn.kv_bytes(sel, HKV, D)
+def reference_inputs(lengths, seed):
+    """One layer of the config-2 workload as CPU torch tensors (bf16 q / caches, int32 table)."""
+    import torch
+
+    gen = torch.Generator().manual_seed(seed)
+    lengths = [int(x) for x in lengths]
+    need = [(L + PS - 1) // PS for L in lengths]
+    pages = sum(need)
+    k = torch.randn((pages, PS, HKV, D), generator=gen, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn((pages, PS, HKV, D), generator=gen, dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((len(lengths), 1, HQ, D), generator=gen, dtype=torch.float32).to(torch.bfloat16)
+    perm = torch.randperm(pages, generator=gen).to(torch.int32)
+    table = torch.zeros((len(lengths), max(need)), dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(need):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    seqlens = torch.tensor(lengths, dtype=torch.int32)
+    return {"q": q, "k_cache": k, "v_cache": v, "block_table": table, "cache_seqlens": seqlens}
 
 
-def time_cpu_oracle(case, reps: int):
-    import oracle
+class CpuBaseline:
+    """Times the reference's CPU implementation of the decode path on this host.
 
-    times = []
-    for _ in range(reps):
-        kc, vc, sl = case.k_cache, case.v_cache, case.cache_seqlens.copy()
+    The reference's own ``flash_attn_with_kvcache`` with its PyTorch fallback
+    (kind "reference", torch threads = every core this process may use); when
+    the reference package is not installed, the numpy oracle port of the same
+    algorithm (kind "port").  One call = one layer of the config-2 batch.
+    """
+
+    def __init__(self, lengths, seed):
+        import torch
+
+        self.lengths = [int(x) for x in lengths]
+        self.cores = host_cores()
+        self.ref = import_reference()
+        self.inputs = reference_inputs(self.lengths, seed)
+        self.nbytes = sum(self.lengths) * HKV * D * 2 * 2
+        torch.set_num_threads(self.cores)
+        if self.ref is not None:
+            self.kind = "reference"
+            self.what = ("reference mxflashattn.flash_attn_with_kvcache (MXFLASHATTN_ALLOW_FALLBACK=1, torch "
+                         f"{torch.__version__} CPU, {self.cores} threads)")
+        else:
+            self.kind = "port"
+            self.what = "numpy fp32 oracle port of the reference's CPU path (reference package not installed)"
+            self.np_inputs = {k: (v.float().numpy() if v.dtype == torch.bfloat16 else v.numpy())
+                              for k, v in self.inputs.items() if v is not None}
+
+    def call(self) -> float:
+        import warnings
+
+        t = self.inputs
         t0 = time.perf_counter()
-        oracle.attention_kvcache(case.q, kc, vc, cache_seqlens=sl, block_table=case.block_table,
-                                 softmax_scale=case.softmax_scale)
-        times.append(time.perf_counter() - t0)
-    return times
+        if self.ref is not None:
+            # the reference reads its fallback switch at call time
+            prev = os.environ.get("MXFLASHATTN_ALLOW_FALLBACK")
+            os.environ["MXFLASHATTN_ALLOW_FALLBACK"] = "1"
+            try:
+                with warnings.catch_warnings():
+                    warnings.simplefilter("ignore", RuntimeWarning)
+                    self.ref.flash_attn_with_kvcache(t["q"], t["k_cache"], t["v_cache"],
+                                                     cache_seqlens=t["cache_seqlens"], block_table=t["block_table"],
+                                                     softmax_scale=D ** -0.5)
+            finally:
+                if prev is None:
+                    del os.environ["MXFLASHATTN_ALLOW_FALLBACK"]
+                else:
+                    os.environ["MXFLASHATTN_ALLOW_FALLBACK"] = prev
+        else:
+            import oracle
+
+            n = self.np_inputs
+            oracle.attention_kvcache(n["q"], n["k_cache"], n["v_cache"], cache_seqlens=n["cache_seqlens"].copy(),
+                                     block_table=n["block_table"], softmax_scale=D ** -0.5)
+        return time.perf_counter() - t0
+
+    def sample(self) -> str:
+        return (f"all {len(self.lengths)} sequences of one layer per call (mean ctx "
+                f"{sum(self.lengths) / len(self.lengths):.1f}), {self.what}, on {cpu_model()}")
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU algorithm (oracle port) on this host's cores."""
+    """--impl reference: the reference's CPU path on this host's cores (rank 0 only)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
     from mxflashattn_b200 import synthetic as syn
 
     lengths = syn.qwen3_4b_lengths(args.seed, args.batch)
-    n_seqs = 16
-    case, nbytes = cpu_oracle_sample(lengths, args.seed, n_seqs)
-    time_cpu_oracle(case, max(1, min(args.warmup, 3)))
-    times = time_cpu_oracle(case, args.steps)
+    base = CpuBaseline(lengths, args.seed)
+    for _ in range(max(1, min(args.warmup, 3))):
+        base.call()
+    times = [base.call() for _ in range(args.steps)]
     sec = sum(times) / len(times)
-    gbs = nbytes / sec / 1e9
-    cores = os.cpu_count() or 1
+    gbs = base.nbytes / sec / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
-                   "head_dim": D, "page_size": PS,
-                   "sample": f"{n_seqs} of {args.batch} sequences of one layer per step"},
-        "tok_per_s": n_seqs / sec / args.layers,
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{n_seqs} sequences x 1 layer per step, numpy fp32 on {cpu_model()}"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 math)", "data": "synthetic",
+        "config": headline_config(args, lengths, world, False),
+        "sample": f"one step = one layer of the {args.batch}-sequence batch (all sequences); GB/s and tok/s "
+                  "scale by the algorithmic bytes of that layer",
+        "tok_per_s": args.batch / sec / args.layers,
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": base.cores, "kind": base.kind,
+                         "sample": base.sample()},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# -------------------------------------------------------------------- ours
+def headline_config(args, lengths, world, fp8):
+    """The ``config`` object of the headline line; both arms print the same one."""
+    import numpy as np
 
-def run_ours(args):
+    bytes_step = int(np.sum(lengths)) * HKV * D * 2 * (1 if fp8 else 2) * args.layers
+    return {"workload": WORKLOAD + (", e4m3 KV cache" if fp8 else ""), "batch": args.batch,
+            "layers": args.layers, "hq": HQ, "hkv": HKV, "head_dim": D, "page_size": PS,
+            "mean_ctx": float(np.mean(lengths)),
+            "l2": f"inputs larger than L2: {args.layers} distinct layer caches, "
+                  f"{bytes_step / 1e9:.1f} GB read per step",
+            "parallelism": f"dp{world} (independent batches, no collective)"}
+
+
+# ------------------------------------------------------------ device helpers
+
+class Ranks:
+    """Process group plumbing: barrier, max-over-ranks reductions (no-ops at N=1)."""
+
+    def __init__(self, world, rank, device):
+        self.world, self.rank, self.device = world, rank, device
+        self.dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=device)
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, values):
+        """Elementwise max over ranks of a list of floats (one collective)."""
+        if self.dist is None:
+            return list(values)
+        import torch
+
+        t = torch.tensor(list(values), device=self.device, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def capture(step, device):
+    """A CUDA graph of ``step()`` (warmed up twice on a side stream first)."""
     import torch
 
-    world, rank, local = dist_env()
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    device = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(device)
-
-    from mxflashattn_b200 import backend, flash_attn_with_kvcache, synthetic as syn
-
-    lengths = syn.qwen3_4b_lengths(args.seed + rank, args.batch)
-    layers = []
-    fp8 = args.kv_dtype == "fp8"
-    for layer in range(args.layers):
-        t = syn.device_paged_decode(seed=1000 * (rank + 1) + layer, lengths=lengths, q_heads=HQ, kv_heads=HKV,
-                                    head_dim=D, dtype="bf16", page_size=PS, device=device)
-        if fp8:  # e4m3 caches at scale 1 (N(0,1) values fit the e4m3 range)
-            t["k_cache"] = t["k_cache"].to(torch.float8_e4m3fn)
-            t["v_cache"] = t["v_cache"].to(torch.float8_e4m3fn)
-        layers.append(t)
-    torch.cuda.synchronize(device)
-    bytes_layer = syn.kv_bytes(lengths, HKV, D, elem_bytes=1 if fp8 else 2)
-    bytes_step = bytes_layer * args.layers
-    max_len = layers[0]["block_table"].shape[1] * PS
-    num_splits, chunk_len = backend.kvcache_plan(args.batch, 1, HQ, HKV, D, max_len)
-    launches_per_layer = 2 if num_splits > 1 else 1
-    scale = D ** -0.5
-    outs = [torch.empty_like(t["q"]) for t in layers]
     stream = torch.cuda.current_stream(device)
-
-    def step(ev=None):
-        for i, t in enumerate(layers):
-            if ev is not None:
-                ev[2 * i].record(stream)
-            backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
-                                      scale, False, num_splits=num_splits, chunk_len=chunk_len, out=outs[i])
-            if ev is not None:
-                ev[2 * i + 1].record(stream)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize(device)
-    barrier()
-    torch.cuda.synchronize(device)
-
-    # The device-resident measurement replays the whole step (36 layers) as one
-    # CUDA graph, so host launch overhead cannot leave the GPU idle between
-    # layers; every kernel of the step runs inside the graph.
     graph = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream(device)
     side.wait_stream(stream)
@@ -292,185 +391,342 @@ def run_ours(args):
     with torch.cuda.graph(graph, stream=side):
         step()
     torch.cuda.synchronize(device)
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
-    torch.cuda.synchronize(device)
-    barrier()
-    torch.cuda.synchronize(device)
+    return graph
 
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(device.index).start()
-    w0 = time.time()
-    t_start.record(stream)
-    for _ in range(args.steps):
+
+def time_graph(graph, steps, warmup, device, ranks, clocks=None):
+    """Device ms of ``steps`` back-to-back replays (after ``warmup``), CUDA events on the launching stream."""
+    import torch
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(warmup, 3)):
         graph.replay()
-    t_end.record(stream)
     torch.cuda.synchronize(device)
-    clocks.mark(w0, time.time())
+    ranks.barrier()
+    torch.cuda.synchronize(device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
+    t0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    if clocks is not None:
+        clocks.mark(w0, time.time())
+    ranks.barrier()
+    return t0.elapsed_time(t1)
+
+
+def build_layers(lengths, seed_base, layers, device, fp8=False):
+    import torch
+
+    from mxflashattn_b200 import synthetic as syn
+
+    out = []
+    for layer in range(layers):
+        t = syn.device_paged_decode(seed=seed_base + layer, lengths=lengths, q_heads=HQ, kv_heads=HKV, head_dim=D,
+                                    dtype="bf16", page_size=PS, device=device)
+        if fp8:  # e4m3 caches at scale 1 (N(0,1) values fit the e4m3 range)
+            t["k_cache"] = t["k_cache"].to(torch.float8_e4m3fn)
+            t["v_cache"] = t["v_cache"].to(torch.float8_e4m3fn)
+        out.append(t)
+    torch.cuda.synchronize(device)
+    return out
+
+
+def decode_graph(layers, device):
+    """(graph, step, outs, plan) for one decode step over ``layers``."""
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    B = layers[0]["q"].shape[0]
+    max_len = layers[0]["block_table"].shape[1] * PS
+    num_splits, chunk_len = backend.kvcache_plan(B, 1, HQ, HKV, D, max_len)
+    outs = [torch.empty_like(t["q"]) for t in layers]
+    scale = D ** -0.5
+
+    def step(ev=None):
+        stream = torch.cuda.current_stream(device)
+        for i, t in enumerate(layers):
+            if ev is not None:
+                ev[2 * i].record(stream)
+            backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                      scale, False, num_splits=num_splits, chunk_len=chunk_len, out=outs[i])
+            if ev is not None:
+                ev[2 * i + 1].record(stream)
+
+    return capture(step, device), step, (num_splits, chunk_len)
+
+
+# -------------------------------------------------------------------- ours
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    ranks = Ranks(world, rank, device)
+
+    from mxflashattn_b200 import flash_attn_with_kvcache, synthetic as syn
+
+    lengths = syn.qwen3_4b_lengths(args.seed + rank, args.batch)
+    fp8 = args.kv_dtype == "fp8"
+    layers = build_layers(lengths, 1000 * (rank + 1), args.layers, device, fp8=fp8)
+    bytes_layer = syn.kv_bytes(lengths, HKV, D, elem_bytes=1 if fp8 else 2)
+    bytes_step = bytes_layer * args.layers
+    stream = torch.cuda.current_stream(device)
+    scale = D ** -0.5
+
+    graph, step, (num_splits, chunk_len) = decode_graph(layers, device)
+    launches_per_layer = 1  # split plans merge in the same launch (counted single launch)
+    clocks = ClockSampler(device.index).start()
+    elapsed_ms = time_graph(graph, args.steps, args.warmup, device, ranks, clocks)
     clocks.stop()
-    barrier()
-    elapsed_ms = t_start.elapsed_time(t_end)
-    # per-launch duration of the decode kernel: the step is nothing but its
-    # launches back to back, so the graph step time divides evenly; with splits
-    # (decode + combine per layer) an event-bracketed eager pass times it alone
-    if launches_per_layer == 1:
-        per_launch_ms = elapsed_ms / args.steps / args.layers
-    else:
+    per_launch_ms = elapsed_ms / args.steps / args.layers
+    if num_splits > 1:  # one event pair per layer: the single launch per layer timed alone
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.layers)]
         step(evs)
         torch.cuda.synchronize(device)
         per_launch_ms = sum(evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(args.layers)) / args.layers
-    if dist is not None:
-        tt = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(tt.item())
+    elapsed_ms = ranks.max([elapsed_ms])[0]
     ms_step = elapsed_ms / args.steps
     value = world * bytes_step / (ms_step * 1e-3) / 1e9
     tok_s = world * args.batch / (ms_step * 1e-3)
+    del graph
 
     # --------------------------------------------------------------- e2e
     e2e = None
     if not args.no_e2e:
-        q_host = [t["q"].cpu().pin_memory() for t in layers]
-        out_host = [torch.empty_like(q, pin_memory=True) for q in q_host]
-        sl_host = layers[0]["cache_seqlens"].cpu().pin_memory()
-        q_dev = [torch.empty_like(t["q"]) for t in layers]
-        # lengths alternate between two device buffers by step parity, so a
-        # step's upload never waits for the previous step's last layer
-        sl_dev = [torch.empty_like(layers[0]["cache_seqlens"]) for _ in range(2)]
-        h2d = torch.cuda.Stream(device)
-        d2h = torch.cuda.Stream(device)
-        ev_in = [torch.cuda.Event() for _ in layers]
-        ev_done = [torch.cuda.Event() for _ in layers]
-        ev_sl = torch.cuda.Event()
-        ev_step = [torch.cuda.Event() for _ in range(2)]
-        parity = [0]
-
-        def e2e_step_tables():
-            # Copies run on their own streams so layer i+1's upload and layer i's
-            # read-back overlap layer i's kernel, and a step's uploads overlap
-            # the previous step's last layers; every copy stays inside the
-            # timed region.  q buffers are reused only after the previous
-            # step's kernel that read them has finished.
-            sl = sl_dev[parity[0]]
-            with torch.cuda.stream(h2d):
-                h2d.wait_event(ev_step[parity[0]])  # the step two back has finished reading this buffer
-                sl.copy_(sl_host, non_blocking=True)
-                ev_sl.record(h2d)
-                for i in range(len(layers)):
-                    h2d.wait_event(ev_done[i])
-                    q_dev[i].copy_(q_host[i], non_blocking=True)
-                    ev_in[i].record(h2d)
-            stream.wait_event(ev_sl)
-            for i, t in enumerate(layers):
-                stream.wait_event(ev_in[i])
-                o = flash_attn_with_kvcache(q_dev[i], t["k_cache"], t["v_cache"], cache_seqlens=sl,
-                                            block_table=t["block_table"], softmax_scale=scale)
-                ev_done[i].record(stream)
-                o.record_stream(d2h)
-                with torch.cuda.stream(d2h):
-                    d2h.wait_event(ev_done[i])
-                    out_host[i].copy_(o, non_blocking=True)
-            ev_step[parity[0]].record(stream)
-            parity[0] ^= 1
-            stream.wait_stream(d2h)  # bounds the read-back backlog (outputs are freed as their copies finish)
-
-        for _ in range(3):
-            e2e_step_tables()
-        torch.cuda.synchronize(device)
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step_tables()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-        barrier()
-        e_ms = e0.elapsed_time(e1)
-        if dist is not None:
-            tt = torch.tensor([e_ms], device=device, dtype=torch.float64)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            e_ms = float(tt.item())
-        e_step = e_ms / args.steps
-        q_bytes = sum(q.numel() * q.element_size() for q in q_host)
-        e2e = {"value": world * bytes_step / (e_step * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": q_bytes + sl_host.numel() * sl_host.element_size(),
-               "d2h_bytes_per_step": sum(o.numel() * o.element_size() for o in out_host),
-               "ms_per_step": e_step, "tok_per_s": world * args.batch / (e_step * 1e-3)}
+        e2e = run_e2e(args, layers, lengths, bytes_step, device, ranks, flash_attn_with_kvcache, scale)
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        case, nbytes = cpu_oracle_sample(lengths, args.seed, 16)
-        time_cpu_oracle(case, 1)
-        times = time_cpu_oracle(case, 3)
+        base = CpuBaseline(syn.qwen3_4b_lengths(args.seed, args.batch), args.seed)
+        base.call()
+        times = [base.call() for _ in range(5)]
         sec = sum(times) / len(times)
-        cpu = {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": f"16 of {args.batch} sequences x 1 layer, numpy fp32 oracle, 3 reps on {cpu_model()}"}
+        cpu = {"value": base.nbytes / sec / 1e9, "unit": "GB/s", "cores": base.cores, "kind": base.kind,
+               "sample": base.sample() + ", mean of 5 timed calls after 1 untimed"}
 
     peak, peak_kind = measured_peaks()
     achieved = bytes_layer / (per_launch_ms * 1e-3) / 1e9
+    traffic = None if fp8 else NCU_TRAFFIC_BYTES.get((args.batch, args.seed))
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 (e4m3 KV cache)" if fp8 else "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD + (", e4m3 KV cache" if fp8 else ""), "batch": args.batch, "layers": args.layers, "hq": HQ, "hkv": HKV,
-                   "head_dim": D, "page_size": PS, "mean_ctx": float(sum(lengths)) / len(lengths),
-                   "num_splits": num_splits, "chunk_len": chunk_len,
-                   "l2": f"inputs larger than L2: {args.layers} distinct layer caches, "
-                         f"{bytes_step / 1e9:.1f} GB read per step",
-                   "parallelism": f"dp{world} (independent batches, no collective)"},
+        "config": headline_config(args, lengths, world, fp8),
+        "plan": {"num_splits": num_splits, "chunk_len": chunk_len},
         "tok_per_s": tok_s,
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak,
-                     "traffic": None if fp8 else NCU_TRAFFIC_BYTES.get((args.batch, args.seed)),
+                     "frac": achieved / peak, "traffic": traffic,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                        "workload (profile value, not measured by this run)") if traffic else None,
                      "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "paged_decode_kernel" + (" + split_combine_kernel" if num_splits > 1 else ""),
-                     "bytes_per_launch": bytes_layer, "avg_launch_ms": per_launch_ms},
+                     "kernel": "paged_decode_kernel", "bytes_per_launch": bytes_layer,
+                     "avg_launch_ms": per_launch_ms},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
         "gpu_launches": args.steps * args.layers * launches_per_layer,
         "timing": "CUDA graph replay of the 36-layer step; e2e is eager through the public API",
     }
+    del layers
+    torch.cuda.empty_cache()
+
+    if not args.no_extras:
+        if not fp8:
+            line["fp8"] = extra_fp8(args, lengths, device, ranks)
+        line["prefill"] = prefill_measure(args, device, ranks, sharded=False, with_cpu=False)
+        if world > 1:
+            line["prefill_heads"] = prefill_measure(args, device, ranks, sharded=True, with_cpu=False)
+            line["strong"] = extra_strong(args, device, ranks)
+        line["longctx"] = extra_longctx(args, device, ranks)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.close()
+
+
+def run_e2e(args, layers, lengths, bytes_step, device, ranks, api, scale):
+    """The headline metric through the public API with host buffers, copies inside the timed region.
+
+    Every step uploads that step's inputs (the 36 layers' q and the lengths)
+    from pinned host memory in one copy and reads the 36 layers' outputs back
+    in one copy.  Device buffers alternate by step parity, so the upload of
+    step s+1 and the read-back of step s-1 run on the copy engines while step
+    s computes; every copy of every timed step lies inside the timed region.
+    """
+    import torch
+
+    world = ranks.world
+    stream = torch.cuda.current_stream(device)
+    q_host = torch.stack([t["q"] for t in layers]).cpu().pin_memory()  # [layers, B, 1, HQ, D]
+    out_host = torch.empty_like(q_host, pin_memory=True)
+    sl_host = layers[0]["cache_seqlens"].cpu().pin_memory()
+    q_dev = [torch.empty_like(q_host, device=device) for _ in range(2)]
+    out_dev = [torch.empty_like(q_host, device=device) for _ in range(2)]
+    sl_dev = [torch.empty_like(layers[0]["cache_seqlens"]) for _ in range(2)]
+    h2d = torch.cuda.Stream(device)
+    d2h = torch.cuda.Stream(device)
+    ev_up = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer p uploaded
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # the step on buffer p finished its kernels
+    ev_down = [torch.cuda.Event() for _ in range(2)]  # outputs of buffer p read back
+    count = [0]
+
+    def e2e_step():
+        p = count[0] & 1
+        count[0] += 1
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(ev_used[p])  # the step two back has finished reading these inputs
+            q_dev[p].copy_(q_host, non_blocking=True)
+            sl_dev[p].copy_(sl_host, non_blocking=True)
+            ev_up[p].record(h2d)
+        stream.wait_event(ev_up[p])
+        stream.wait_event(ev_down[p])  # ... and its outputs have left this buffer
+        for i, t in enumerate(layers):
+            api(q_dev[p][i], t["k_cache"], t["v_cache"], cache_seqlens=sl_dev[p], block_table=t["block_table"],
+                softmax_scale=scale, out=out_dev[p][i])
+        ev_used[p].record(stream)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev_used[p])
+            out_host.copy_(out_dev[p], non_blocking=True)
+            ev_down[p].record(d2h)
+
+    for _ in range(4):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    ranks.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    h0 = time.perf_counter()
+    e0.record(stream)
+    h2d.wait_stream(stream)  # the first upload starts inside the timed region
+    for _ in range(args.steps):
+        e2e_step()
+    stream.wait_stream(d2h)  # the last read-back ends inside the timed region
+    e1.record(stream)
+    host_s = time.perf_counter() - h0  # host time to enqueue every step (no synchronisation inside)
+    torch.cuda.synchronize(device)
+    ranks.barrier()
+    e_ms = e0.elapsed_time(e1)
+
+    # the copy engines alone: one step's upload, then its read-back
+    c = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize(device)
+    c[0].record(h2d)
+    with torch.cuda.stream(h2d):
+        q_dev[0].copy_(q_host, non_blocking=True)
+    c[1].record(h2d)
+    c[2].record(d2h)
+    with torch.cuda.stream(d2h):
+        d2h.wait_event(c[1])
+        out_host.copy_(out_dev[0], non_blocking=True)
+    c[3].record(d2h)
+    torch.cuda.synchronize(device)
+    h2d_ms, d2h_ms = c[0].elapsed_time(c[1]), c[1].elapsed_time(c[3])
+    e_ms, host_ms = ranks.max([e_ms, host_s * 1e3])
+    e_step = e_ms / args.steps
+    q_bytes = q_host.numel() * q_host.element_size()
+    o_bytes = out_host.numel() * out_host.element_size()
+    return {"value": world * bytes_step / (e_step * 1e-3) / 1e9, "unit": "GB/s",
+            "h2d_bytes_per_step": q_bytes + sl_host.numel() * sl_host.element_size(),
+            "d2h_bytes_per_step": o_bytes, "ms_per_step": e_step,
+            "tok_per_s": world * args.batch / (e_step * 1e-3),
+            "host_ms_per_step": host_ms / args.steps,
+            "host_us_per_call": host_ms * 1e3 / (args.steps * len(layers)),
+            "h2d_gbs_alone": q_bytes / (h2d_ms * 1e-3) / 1e9 if h2d_ms > 0 else None,
+            "d2h_gbs_alone": o_bytes / (d2h_ms * 1e-3) / 1e9 if d2h_ms > 0 else None,
+            "method": "public flash_attn_with_kvcache per layer (out= a slot of the step's output buffer), eager; "
+                      "per step one upload of every layer's q and the lengths and one read-back of every layer's "
+                      "output, on copy streams overlapping the neighbouring steps' kernels; *_gbs_alone = one "
+                      "step's copies timed alone"}
+
+
+def extra_fp8(args, lengths, device, ranks):
+    """The headline workload over e4m3 caches (k_scale = v_scale = 1)."""
+    import torch
+
+    from mxflashattn_b200 import synthetic as syn
+
+    layers = build_layers(lengths, 1000 * (ranks.rank + 1), args.layers, device, fp8=True)
+    graph, _, (num_splits, _) = decode_graph(layers, device)
+    ms = time_graph(graph, args.steps, args.warmup, device, ranks)
+    per_launch = ms / args.steps / args.layers
+    ms = ranks.max([ms])[0]
+    del graph, layers
+    torch.cuda.empty_cache()
+    bytes_layer = syn.kv_bytes(lengths, HKV, D, elem_bytes=1)
+    ms_step = ms / args.steps
+    peak, kind = measured_peaks()
+    achieved = bytes_layer / (per_launch * 1e-3) / 1e9
+    return {"metric": "decode-attn KV HBM GB/s, e4m3 KV cache (config 2 shape)",
+            "value": ranks.world * bytes_layer * args.layers / (ms_step * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms_step, "tok_per_s": ranks.world * args.batch / (ms_step * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{kind} hbm_gbs",
+                         "bytes_per_launch": bytes_layer, "bytes_rule": "1 B per cached e4m3 element"},
+            "num_splits": num_splits, "gpu_launches": args.steps * args.layers}
+
+
+def extra_strong(args, device, ranks):
+    """The one config-2 batch of 128 sequences split 128/N per rank (no collective)."""
+    import torch
+
+    from mxflashattn_b200 import context_split as cs, synthetic as syn
+
+    all_lengths = syn.qwen3_4b_lengths(args.seed, args.batch)
+    mine = cs.shard_batch(args.batch, ranks.world, ranks.rank)
+    lengths = all_lengths[mine.start:mine.stop]
+    layers = build_layers(lengths, 5000 + 100 * ranks.rank, args.layers, device)
+    graph, _, (num_splits, _) = decode_graph(layers, device)
+    ms = ranks.max([time_graph(graph, args.steps, args.warmup, device, ranks)])[0]
+    del graph, layers
+    torch.cuda.empty_cache()
+    total = syn.kv_bytes(all_lengths, HKV, D) * args.layers
+    ms_step = ms / args.steps
+    return {"metric": "decode-attn KV HBM GB/s, config-2 batch of 128 split over the ranks",
+            "value": total / (ms_step * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_step,
+            "tok_per_s": args.batch / (ms_step * 1e-3), "scaling": "strong",
+            "sequences_per_rank": len(lengths), "num_splits": num_splits}
 
 
 # ------------------------------------------------------------------ prefill
 
-def run_prefill(args):
-    """Config 5 prefill: causal flash_attn_varlen_func over packed sequences (1 GPU per rank, weak scaling)."""
+def prefill_measure(args, device, ranks, *, sharded: bool, with_cpu: bool):
+    """Config 5 prefill: causal flash_attn_varlen_func over packed sequences.
+
+    ``sharded``: each rank runs the KV heads ``shard_kv_heads(HKV, N, rank)``
+    of the one batch (strong scaling); otherwise every rank runs the whole
+    batch (weak scaling).
+    """
     import numpy as np
     import torch
 
-    world, rank, local = dist_env()
-    dist = None
-    if world > 1:
-        import datetime
+    from mxflashattn_b200 import backend, context_split as cs, flash_attn_varlen_func
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    device = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(device)
-    from mxflashattn_b200 import flash_attn_varlen_func, backend
-
+    world, rank = ranks.world, ranks.rank
     lens = [int(x) for x in args.prefill_lens.split(",")]
     total = sum(lens)
+    heads = cs.shard_kv_heads(HKV, world, rank) if sharded else range(HKV)
+    hkv = len(heads)
+    hq = hkv * (HQ // HKV)
     gen = torch.Generator(device=device)
-    gen.manual_seed(args.seed + rank)
+    gen.manual_seed(args.seed + (0 if sharded else rank))
     q = torch.randn((total, HQ, D), generator=gen, device=device, dtype=torch.bfloat16)
     k = torch.randn((total, HKV, D), generator=gen, device=device, dtype=torch.bfloat16)
     v = torch.randn((total, HKV, D), generator=gen, device=device, dtype=torch.bfloat16)
+    if sharded:
+        g = HQ // HKV
+        q = q[:, heads.start * g:heads.stop * g].contiguous()
+        k = k[:, heads.start:heads.stop].contiguous()
+        v = v[:, heads.start:heads.stop].contiguous()
     cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=device)
-    flops = 4 * HQ * D * sum(L * (L + 1) // 2 for L in lens)
+    flops_rank = 4 * hq * D * sum(L * (L + 1) // 2 for L in lens)
+    flops_job = flops_rank * world if not sharded else 4 * HQ * D * sum(L * (L + 1) // 2 for L in lens)
     scale = D ** -0.5
     stream = torch.cuda.current_stream(device)
 
@@ -480,8 +736,7 @@ def run_prefill(args):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(device)
-    if dist is not None:
-        dist.barrier()
+    ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(device.index).start()
     w0 = time.time()
@@ -492,44 +747,41 @@ def run_prefill(args):
     torch.cuda.synchronize(device)
     clocks.mark(w0, time.time())
     clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    if dist is not None:
-        tt = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    tflops = world * flops / (ms * 1e-3) / 1e12
+    ms_local = e0.elapsed_time(e1) / args.steps
 
-    e2e = None
+    e2e_ms = None
+    hq_b = hk_b = None
     if not args.no_e2e:  # public API with host inputs: q/k/v and cu_seqlens uploaded, output read back
-        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hq_b, hk_b, hv_b = (t.cpu().pin_memory() for t in (q, k, v))
         hcu = cu.cpu()
-        hout = torch.empty_like(hq, pin_memory=True)
+        hout = torch.empty_like(hq_b, pin_memory=True)
 
         def e2e_step():
-            dq, dk, dv = (t.to(device, non_blocking=True) for t in (hq, hk, hv))
+            dq, dk, dv = (t.to(device, non_blocking=True) for t in (hq_b, hk_b, hv_b))
             dcu = hcu.to(device, non_blocking=True)
             out = flash_attn_varlen_func(dq, dk, dv, dcu, dcu, max(lens), max(lens), causal=True)
             hout.copy_(out, non_blocking=True)
 
         e2e_step()
         torch.cuda.synchronize(device)
+        ranks.barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(args.steps):
             e2e_step()
         f1.record(stream)
         torch.cuda.synchronize(device)
-        ems = f0.elapsed_time(f1) / args.steps
-        if dist is not None:
-            tt = torch.tensor([ems], device=device, dtype=torch.float64)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            ems = float(tt.item())
-        e2e = {"value": world * flops / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hq, hk, hv, hcu)),
-               "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": ems}
+        e2e_ms = f0.elapsed_time(f1) / args.steps
+        h2d = sum(t.numel() * t.element_size() for t in (hq_b, hk_b, hv_b, hcu))
+        d2h = hout.numel() * hout.element_size()
+    ms, e2e_ms_max = ranks.max([ms_local, e2e_ms if e2e_ms is not None else 0.0])
+    e2e = None
+    if e2e_ms is not None:
+        e2e = {"value": flops_job / (e2e_ms_max * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms_max}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if with_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
         from mxflashattn_b200 import synthetic as syn
 
@@ -539,28 +791,142 @@ def run_prefill(args):
         oracle.attention_varlen(c.q, c.k, c.v, c.cu_q, c.cu_k, causal=True)
         sec = time.perf_counter() - t0
         sflops = 4 * HQ * D * sum(L * (L + 1) // 2 for L in sample)
-        cpu = {"value": sflops / sec / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+        cpu = {"value": sflops / sec / 1e12, "unit": "TFLOP/s", "cores": host_cores(), "kind": "port",
                "sample": f"sequences {sample} of the batch, numpy fp32 oracle on {cpu_model()}"}
 
     peak, kind = measured_tensor_peak()
-    per_gpu = flops / (ms * 1e-3) / 1e12
-    line = {
-        "metric": "causal varlen prefill forward TFLOP/s (config 5)", "value": tflops, "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "prefill varlen causal (config 5)", "lengths": lens, "hq": HQ, "hkv": HKV,
-                   "head_dim": D, "flops_per_step": flops, "l2": "q/k/v 0.08 GB reused from L2 by design "
-                   "(compute-bound kernel)", "parallelism": f"dp{world}"},
+    per_gpu = flops_rank / (ms_local * 1e-3) / 1e12
+    return {
+        "metric": "causal varlen prefill forward TFLOP/s (config 5)"
+                  + (", KV-head groups split over the ranks" if sharded else ""),
+        "value": flops_job / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "prefill varlen causal (config 5)", "lengths": lens, "hq": hq, "hkv": hkv,
+                   "head_dim": D, "flops_per_step": flops_job,
+                   "l2": "q/k/v 0.08 GB reused from L2 by design (compute-bound kernel)",
+                   "parallelism": (f"KV heads {heads.start}..{heads.stop - 1} on this rank" if sharded
+                                   else f"dp{world}")},
         "e2e": e2e,
         "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                      "frac": per_gpu / peak, "traffic": None, "peak_source": kind, "kernel": "prefill_tc_kernel"},
         "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps,
     }
+
+
+def run_prefill(args):
+    """--workload prefill: config 5 as the line's own metric (weak scaling over ranks)."""
+    import torch
+
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    ranks = Ranks(world, rank, device)
+    line = prefill_measure(args, device, ranks, sharded=False, with_cpu=True)
+    line["warmup"] = args.warmup
+    line["vs_baseline"] = None
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.close()
+
+
+# ------------------------------------------------------- long-context decode
+
+def extra_longctx(args, device, ranks):
+    """Config 5 decode: 16384-token contexts, B=8 and B=1, 36 layers.
+
+    N=1: the one-GPU split decode (the baseline the context split is compared
+    with).  N>1: each rank holds a page-aligned range of every sequence
+    (``context_split.local_view``) and the per-rank (O, LSE) records are
+    exchanged once per layer: (a) fused into the kernels over NVLink peer
+    memory (``FusedContextParallelDecode``), (b) by one NCCL all-gather plus
+    the local merge kernel (``context_parallel_decode``).  Both run as CUDA
+    graph replays of the 36-layer step.  Layer 0's merged output and LSE of
+    both forms are checked on every rank against a one-GPU decode over the
+    whole context; device error flags are read on every rank.
+    """
+    import torch
+
+    from mxflashattn_b200 import _lib, backend, context_split as cs, synthetic as syn
+
+    world = ranks.world
+    scale = D ** -0.5
+    peak, kind = measured_peaks()
+    res = {"metric": "long-context decode, KV HBM GB/s (config 5: ctx 16384, Hq32/Hk8/D128 bf16)",
+           "unit": "GB/s", "layers": args.layers}
+    for B in LONG_BATCHES:
+        lengths = [LONG_CTX] * B
+        full = build_layers(lengths, 90000 + 1000 * B, args.layers, device)  # identical on every rank
+        bytes_layer = syn.kv_bytes(lengths, HKV, D)
+        entry = {"batch": B, "bytes_per_layer": bytes_layer}
+        if world == 1:
+            graph, _, (ns, _) = decode_graph(full, device)
+            ms = time_graph(graph, args.steps, args.warmup, device, ranks)
+            del graph
+            us = ms * 1e3 / args.steps / args.layers
+            entry.update({"us_per_layer": us, "value": bytes_layer / (us * 1e-6) / 1e9,
+                          "frac": bytes_layer / (us * 1e-6) / 1e9 / peak, "num_splits": ns,
+                          "form": "one-GPU split decode (single launch per layer)"})
+        else:
+            locs = []
+            for t in full:
+                ll, table = cs.local_view(t["cache_seqlens"].cpu().numpy(), t["block_table"].cpu().numpy(), world,
+                                          ranks.rank, PS)
+                locs.append((torch.from_numpy(ll).to(device), torch.from_numpy(table).to(device)))
+            fused = cs.FusedContextParallelDecode(B, HQ, HKV, D, device=device)
+            outs_f = [None] * len(full)
+            outs_n = [None] * len(full)
+
+            def step_fused():
+                for i, t in enumerate(full):
+                    outs_f[i] = fused(t["q"], t["k_cache"], t["v_cache"], locs[i][0], locs[i][1], scale)
+
+            def step_nccl():
+                for i, t in enumerate(full):
+                    outs_n[i] = cs.context_parallel_decode(t["q"], t["k_cache"], t["v_cache"], locs[i][0],
+                                                           locs[i][1], scale)
+
+            g_f = capture(step_fused, device)
+            ms_f = time_graph(g_f, args.steps, args.warmup, device, ranks)
+            g_n = capture(step_nccl, device)
+            ms_n = time_graph(g_n, args.steps, args.warmup, device, ranks)
+            torch.cuda.synchronize(device)
+            # parity of layer 0 against the one-GPU decode over the whole context (eager calls)
+            t0 = full[0]
+            ref, ref_lse = backend.kvcache_attention(t0["q"], t0["k_cache"], t0["v_cache"], t0["cache_seqlens"],
+                                                     t0["block_table"], scale, False, return_lse=True)
+            of, lf = fused(t0["q"], t0["k_cache"], t0["v_cache"], locs[0][0], locs[0][1], scale, return_lse=True)
+            on, ln = cs.context_parallel_decode(t0["q"], t0["k_cache"], t0["v_cache"], locs[0][0], locs[0][1],
+                                                scale, return_lse=True)
+            torch.cuda.synchronize(device)
+            err_f = float((of.float() - ref.float()).abs().max())
+            err_n = float((on.float() - ref.float()).abs().max())
+            lerr_f = float((lf.reshape(-1) - ref_lse.reshape(-1)).abs().max())
+            lerr_n = float((ln.reshape(-1) - ref_lse.reshape(-1)).abs().max())
+            flags = float(_lib.read_error_flags())
+            del g_f, g_n
+            fused.close()
+            ms_f, ms_n, err_f, err_n, lerr_f, lerr_n, flags = ranks.max([ms_f, ms_n, err_f, err_n, lerr_f, lerr_n,
+                                                                          flags])
+            us_f = ms_f * 1e3 / args.steps / args.layers
+            us_n = ms_n * 1e3 / args.steps / args.layers
+            entry.update({
+                "us_per_layer_fused": us_f, "us_per_layer_nccl": us_n,
+                "value": bytes_layer / (us_f * 1e-6) / 1e9,
+                "value_nccl": bytes_layer / (us_n * 1e-6) / 1e9,
+                "frac_of_n_gpu_peak": bytes_layer / (us_f * 1e-6) / 1e9 / (peak * world),
+                "max_abs_err_fused": err_f, "max_abs_err_nccl": err_n,
+                "lse_err_fused": lerr_f, "lse_err_nccl": lerr_n,
+                "tolerance": {"out": 1e-2, "lse": 1e-3, "against": "one-GPU decode over the whole context"},
+                "parity_ok": bool(max(err_f, err_n) <= 1e-2 and max(lerr_f, lerr_n) <= 1e-3 and flags == 0),
+                "device_flags": int(flags),
+                "form": "fused NVLink peer-store exchange vs NCCL all-gather + merge, CUDA graph replay",
+                "gpu_launches_fused": args.steps * args.layers * 2,
+            })
+        res[f"b{B}"] = entry
+        del full
+        torch.cuda.empty_cache()
+    return res
 
 
 def main():

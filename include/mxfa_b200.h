@@ -72,8 +72,14 @@ int mxfa_read_error_flags(unsigned int* flags);
  * (m1_kernel.cpp:862-888) merges, and this call runs that combine too.
  * Guards as the reference: D in {64,128}, HQ % HKV == 0, GQ in {2,4,8},
  * NP >= 1, else -1.  `um` (the reference's softmax-variant switch, 0/1/2)
- * is accepted and validated; every variant is served by the same
- * overflow-safe online softmax here. */
+ * is ignored, as the reference launcher never rejects it either: every
+ * variant is served by the same overflow-safe online softmax here.
+ * Page indices are NOT bounded on this entry: the reference ABI carries no
+ * page count, so the tensor maps span every slot row a 32-bit index can
+ * name, and a corrupt block-table entry reads outside the caches (as it
+ * would in the reference).  Callers that cannot vouch for their tables use
+ * mxfa_kvcache_attention_launch, whose num_pages bounds every entry
+ * (out-of-range entries read zeros and raise MXFA_FLAG_PAGE_OUT_OF_RANGE). */
 int mxfa_paged_decode_split_launch(const void* q, const void* k, const void* v, const void* bt,
                                    const void* sl, void* out, void* ows, void* mdws, float scale,
                                    int B, int HQ, int HKV, int D, int PS, int BTW, int bf16, int NP,

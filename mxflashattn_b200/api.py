@@ -138,16 +138,20 @@ def flash_attn_with_kvcache(
     *,
     k_scale: float | None = None,
     v_scale: float | None = None,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Paged or dense KV-cache attention with optional append (api.py:151-286).
 
     Appending ``k``/``v`` writes the caches and advances ``cache_seqlens`` in
     place on the device, like the reference.
 
-    Extension beyond the reference: ``k_cache``/``v_cache`` may be
-    ``torch.float8_e4m3fn`` (head dim 128, q in fp16/bf16); the attended
-    values are ``k_cache * k_scale`` and ``v_cache * v_scale`` (default 1.0).
-    Appended ``k``/``v`` must then already be e4m3 with the same scales.
+    Extensions beyond the reference (keyword-only, so every reference call is
+    unchanged): ``k_cache``/``v_cache`` may be ``torch.float8_e4m3fn`` (head
+    dim 128, q in fp16/bf16); the attended values are ``k_cache * k_scale``
+    and ``v_cache * v_scale`` (default 1.0), and appended ``k``/``v`` must
+    then already be e4m3 with the same scales.  ``out`` (contiguous, q's
+    shape, dtype and device) receives the result instead of a new tensor and
+    is returned.
     """
     validate_softmax_scale(softmax_scale)
     if rotary_cos is not None or rotary_sin is not None:
@@ -209,12 +213,17 @@ def flash_attn_with_kvcache(
             raise ValueError("block_table must be on the same device as q")
     elif k_cache.shape[0] != q.shape[0]:
         raise ValueError("dense cache batch dimension must match q")
+    if out is not None and (not isinstance(out, torch.Tensor) or out.shape != q.shape or out.dtype != q.dtype
+                            or out.device != q.device or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous tensor with q's shape, dtype and device")
     if os.getenv("MXFLASHATTN_STRICT_VALIDATION", "0") == "1":
         _strict_kvcache_checks(k_cache, k, cache_seqlens, block_table)
     args = (q, k_cache, v_cache, k, v, cache_seqlens, block_table, _resolved_scale(q.shape[-1], softmax_scale),
             causal)
-    if fp8_cache:
+    if fp8_cache or out is not None:
         args += (1.0 if k_scale is None else float(k_scale), 1.0 if v_scale is None else float(v_scale))
+    if out is not None:
+        args += (out,)
     return dispatch("flash_attn_with_kvcache", q, args)
 
 

@@ -281,31 +281,32 @@ def seqlens_add_(cache_seqlens: torch.Tensor, delta: int) -> None:
 
 
 def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, softmax_scale, causal,
-                            k_scale: float = 1.0, v_scale: float = 1.0):
+                            k_scale: float = 1.0, v_scale: float = 1.0, out=None):
     """``flash_attn_with_kvcache`` semantics of the reference (reference.py:88-139).
 
     Appends ``k``/``v`` (when given) at the current lengths, attends over the
     grown cache, then advances ``cache_seqlens`` in place -- all on the
-    current stream, with no host synchronisation.
+    current stream, with no host synchronisation.  ``out`` (optional, q's
+    shape and dtype, contiguous) receives the result.
     """
     if q.shape[1] == 0:
         if k is not None:
             kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
             seqlens_add_(cache_seqlens, k.shape[1])
-        return torch.empty_like(q)
+        return out if out is not None else torch.empty_like(q)
     append_len = 0
     if k is not None and fused_append_supported(q, k_cache, k):
         # decode shapes: the attention kernel writes the new rows itself (one launch fewer)
         append_len = k.shape[1]
         out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
-                                append_len=append_len, k_new=k, v_new=v)
+                                append_len=append_len, k_new=k, v_new=v, out=out)
         seqlens_add_(cache_seqlens, append_len)
         return out
     if k is not None:
         kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
         append_len = k.shape[1]
     out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
-                            append_len=append_len, k_scale=k_scale, v_scale=v_scale)
+                            append_len=append_len, k_scale=k_scale, v_scale=v_scale, out=out)
     if k is not None:
         seqlens_add_(cache_seqlens, append_len)
     return out

@@ -679,7 +679,10 @@ int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cach
 int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int B, int HQ, int HKV, int D, int bf16,
                          void* stream) {
   if (local_buf == nullptr || out == nullptr) return fail(MXFA_ERR_INVALID, "null pointer");
-  if (world < 1 || HKV <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return fail(MXFA_ERR_INVALID, "bad geometry");
+  // the merge checks one rank's flag per lane of a warp: at most 32 ranks,
+  // as mxfa_cp_decode_launch
+  if (world < 1 || world > 32) return fail(MXFA_ERR_INVALID, "world %d outside 1..32 ranks", world);
+  if (HKV <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return fail(MXFA_ERR_INVALID, "bad geometry");
   if (B <= 0) return MXFA_OK;
   const int rows = B * HQ;
   cudaLaunchConfig_t cfg{};
@@ -917,8 +920,10 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
 // The buffer is a file-scope __device__ array, so every GPU that loads the
 // library holds MXFA_NOALLOC_SCRATCH_BYTES of it until the process exits.
 // Its name is only a host-side stand-in: the device address is obtained with
-// cudaGetSymbolAddress, once per device, with that device current, on the
-// first call made on that device.  All calls on a device share the buffer and
+// cudaGetSymbolAddress with the device current, on the first call made on
+// that device, and again whenever that device's context has changed since
+// (a cudaDeviceReset tears the module down, and the re-created context may
+// place the array elsewhere).  All calls on a device share the buffer and
 // leave their partials in it; nothing needs to start at zero because the
 // decode kernel writes every partial slot the combine kernel then reads.
 namespace mxfa {
@@ -926,21 +931,52 @@ namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[MXFA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
+// Process-unique id of the calling thread's current context (0 if none or
+// the driver cannot say).  Context ids are never reused within a process,
+// unlike context handles.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
 int noalloc_scratch(float** out) {
   static float* addr[64] = {};
+  static unsigned long long ctx_id[64] = {};
   static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(MXFA_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  const unsigned long long id = current_context_id();
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  if (addr[dev] == nullptr || id == 0 || id != ctx_id[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(MXFA_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
                   cudaGetErrorString(e));
     addr[dev] = static_cast<float*>(p);
+    // the lookup makes the device's context current if nothing was yet
+    ctx_id[dev] = current_context_id();
   }
   *out = addr[dev];
   return MXFA_OK;
@@ -955,15 +991,22 @@ extern "C" int mxfa_kvcache_attention_noalloc_launch(const void* q, const void* 
                                                      int BTW, int num_pages, int append_len, int num_splits,
                                                      int chunk_len, int causal, int bf16, float scale,
                                                      void* stream) {
-  if (B <= 0 || Sq <= 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0 || PS <= 0)
-    return mxfa_kvcache_attention_launch(q, k_cache, v_cache, block_table, seqlens, out, lse, nullptr, 0, B, Sq,
-                                         HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal,
-                                         bf16, scale, stream);
+  // The same argument checks as the workspace entry point, first, so a bad
+  // argument is reported as itself and never as a scratch-size refusal.
+  if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
+  if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
+    return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
+  if (B == 0 || Sq == 0) return MXFA_OK;
+  if (PS <= 0 || num_pages <= 0 || append_len < 0) return fail(MXFA_ERR_INVALID, "bad cache geometry");
+  if (block_table != nullptr && BTW <= 0) return fail(MXFA_ERR_INVALID, "block table width must be positive");
+  if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  const long long rows = static_cast<long long>(B) * Sq * HQ;
+  if (rows > 0x7FFFFFFFll) return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows exceed the 32-bit row index", rows);
   const int max_len = block_table ? BTW * PS : PS;
   if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
   float* scratch = nullptr;
   if (num_splits > 1) {
-    const size_t need = mxfa_split_workspace_bytes(B * Sq * HQ, D, num_splits);
+    const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
     if (need > MXFA_NOALLOC_SCRATCH_BYTES)
       return fail(MXFA_ERR_UNSUPPORTED,
                   "allocation-free call needs %zu bytes of split scratch but the built-in buffer holds %u; "

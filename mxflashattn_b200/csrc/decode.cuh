@@ -1077,7 +1077,10 @@ __global__ void __launch_bounds__(128) cp_merge_kernel(unsigned char* buf, T* __
     const unsigned long long t0 = global_timer_ns();
     while (!__all_sync(0xffffffffu, ready)) {
       if (!ready) ready = ld_acquire_sys(flags + static_cast<size_t>(lane) * units + unit) == epoch + 1u;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      // lane 0's clock decides for the whole warp, so every lane leaves the
+      // loop together and the next __all_sync is always warp-complete
+      const bool late = __shfl_sync(0xffffffffu, global_timer_ns() - t0 > kWaitLimitNs, 0);
+      if (late) {
         if (lane == 0) raise_flag(MXFA_FLAG_WAIT_TIMEOUT);
         break;
       }

@@ -239,3 +239,24 @@ def test_fp8_scales_reach_the_backend(monkeypatch):
     q, kc, vc, sl, bt = _fp8_paged()
     assert flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt, k_scale=0.5, v_scale=2.0) == "result"
     assert calls[0][-2:] == (0.5, 2.0)
+
+
+def test_out_buffer_is_validated_and_passed_to_the_backend(monkeypatch):
+    calls = []
+    ext = SimpleNamespace(is_available=lambda: True,
+                          flash_attn_with_kvcache=lambda *args: calls.append(args) or args[-1])
+    monkeypatch.setattr(dispatch, "_native_extension", lambda: ext)
+    monkeypatch.setattr(dispatch, "native_unavailable_reason", lambda tensor, op: None)
+    q, k, v = tensors()
+    sl = torch.tensor([3], dtype=torch.int32)
+    with pytest.raises(ValueError, match="out must be"):
+        flash_attn_with_kvcache(q, k, v, cache_seqlens=sl, out=torch.empty(1, 1, 2, 64, dtype=q.dtype))
+    with pytest.raises(ValueError, match="out must be"):
+        flash_attn_with_kvcache(q, k, v, cache_seqlens=sl, out=torch.empty_like(q, dtype=torch.bfloat16))
+    assert not calls
+    out = torch.empty_like(q)
+    assert flash_attn_with_kvcache(q, k, v, cache_seqlens=sl, out=out) is out
+    assert calls[0][-3:-1] == (1.0, 1.0) and calls[0][-1] is out
+    # without `out` the backend receives the reference's nine positional arguments
+    flash_attn_with_kvcache(q, k, v, cache_seqlens=sl)
+    assert len(calls[1]) == 9

@@ -127,6 +127,26 @@ def test_paged_kv_cache_reads_blocks_in_table_order(cuda_device):
     torch.testing.assert_close(out, expected, rtol=0, atol=2e-3)
 
 
+def test_out_buffer_receives_the_same_result(cuda_device):
+    """The keyword-only ``out`` extension writes the result in place, bit for bit."""
+    import torch
+
+    from mxflashattn_b200 import flash_attn_with_kvcache
+
+    torch.manual_seed(6)
+    q = torch.randn(3, 1, 8, 128, device=cuda_device, dtype=torch.bfloat16)
+    kc = torch.randn(40, 16, 2, 128, device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.randperm(39, device=cuda_device).to(torch.int32).reshape(3, 13)
+    sl = torch.tensor([200, 17, 1], dtype=torch.int32, device=cuda_device)
+    ref = flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt)
+    out = torch.full_like(q, float("nan"))
+    got = flash_attn_with_kvcache(q, kc, vc, cache_seqlens=sl, block_table=bt, out=out)
+    torch.cuda.synchronize()
+    assert got is out
+    assert torch.equal(out, ref)
+
+
 def test_strict_validation_rejects_out_of_range_page(monkeypatch, cuda_device):
     import torch
 

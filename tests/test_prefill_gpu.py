@@ -39,6 +39,22 @@ def test_varlen_matches_reference_goldens(name, golden, cuda_device):
                      extra=p_rounding_bound(case.dtype, abs_v))
 
 
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_varlen_normal_inputs_within_north_star_bound_without_allowance(dt, d, cuda_device):
+    """Config 5's value distribution (q, k, v ~ N(0,1)) over several key tiles, every row and head against the
+    fp32 oracle at the plain north-star bound: max-abs 2e-3 (fp16) / 1e-2 (bf16), no P-rounding allowance."""
+    from mxflashattn_b200 import flash_attn_varlen_func
+
+    case = syn.varlen_case(70 + d, q_lens=[300, 77, 1000], q_heads=8, kv_heads=2, head_dim=d, dtype=dt,
+                           causal=True)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out = flash_attn_varlen_func(q, k, v, cu_q, cu_k, 1000, 1000, causal=True)
+    ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, softmax_scale=case.softmax_scale,
+                                  causal=True)
+    assert_close_out(host(out), ref, dt, f"N(0,1) {dt} d{d} (strict)")
+
+
 @pytest.mark.parametrize("name", ["varlen_causal_bf16", "varlen_causal_d128_gq4"])
 def test_varlen_lse(name, golden, cuda_device):
     from mxflashattn_b200 import backend
