@@ -893,17 +893,17 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
       !encode_rows_map(&mv, v, D, HKV, total_k, kTcKeys))
     return fail(MXFA_ERR_UNSUPPORTED, "TMA descriptor encoding failed for the prefill operands");
   dim3 grid(HQ, B, (max_q + kTcRows - 1) / kTcRows);
-  auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done) -> int {
+  auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done, int threads) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;
-    kern<<<grid, kTcThreads, smem, st>>>(p, mq, mk, mv);
+    kern<<<grid, threads, smem, st>>>(p, mq, mk, mv);
     return check_launch("prefill_tc_kernel");
   };
   static std::atomic<unsigned long long> d0{0}, d1{0}, d2{0}, d3{0};
   if (bf16)
-    return D == 128 ? go(prefill_tc_kernel<__nv_bfloat16, 128>, TcCfg<128>::kSmemBytes, d0)
-                    : go(prefill_tc_kernel<__nv_bfloat16, 64>, TcCfg<64>::kSmemBytes, d1);
-  return D == 128 ? go(prefill_tc_kernel<__half, 128>, TcCfg<128>::kSmemBytes, d2)
-                  : go(prefill_tc_kernel<__half, 64>, TcCfg<64>::kSmemBytes, d3);
+    return D == 128 ? go(prefill_tc_kernel<__nv_bfloat16, 128>, TcCfg<128>::kSmemBytes, d0, TcCfg<128>::kThreads)
+                    : go(prefill_tc_kernel<__nv_bfloat16, 64>, TcCfg<64>::kSmemBytes, d1, TcCfg<64>::kThreads);
+  return D == 128 ? go(prefill_tc_kernel<__half, 128>, TcCfg<128>::kSmemBytes, d2, TcCfg<128>::kThreads)
+                  : go(prefill_tc_kernel<__half, 64>, TcCfg<64>::kSmemBytes, d3, TcCfg<64>::kThreads);
 }
 
 }  // extern "C"

@@ -2,25 +2,19 @@
 // (tcgen05 MMA, accumulators in tensor memory, operands staged by TMA).
 //
 // CTA = one 128-row query tile of one head; 12 warps, specialised:
-//   warp 0    : TMA producer -- Q once, then K and V tiles (128 keys) into a
-//               three-stage ring, each stage guarded by full/empty mbarriers
-//   warp 1    : allocates tensor memory and issues every tcgen05.mma from one
-//               thread:  S_j = Q K_j^T   (M=128, N=128, K=D; both K-major)
-//                        O_{j%2} += P_j V_j (M=128, N=D, K=128; P from tensor
-//                        memory, V MN-major), committing each to an mbarrier
+//   warp 0    : TMA producer -- Q once, then K and V tiles (128 keys) into
+//               three-stage rings, in the order the tensor pipe consumes them
+//   warp 1    : allocates tensor memory; issues the P.V products
+//               O += P_j V_j (M=128, N=D, K=128; P from tensor memory, V MN-major)
+//   warp 2    : issues the score products S_j = Q K_j^T (M=128, N=128, K=D)
 //   warps 4-7 : softmax group 0 -- key tiles 0, 2, 4, ...
 //   warps 8-11: softmax group 1 -- key tiles 1, 3, 5, ...
-// Each softmax group keeps its own online state (m, l) and its own output
-// accumulator O_g in tensor memory, like two interleaved splits of the key
-// range; the groups merge (m, l, O) once at the end.  Two groups put two
-// softmax warps on every SM sub-partition, so one warp's exp2 / conversion
-// latency overlaps the other's work, and the tensor pipe always has the other
-// group's products queued.  Per tile a group makes two passes over S in
-// tensor memory (row max, then exp2 + sum + bf16/fp16 pack), writing P_j over
-// the columns of S_j it has already read.
-// Tensor memory: S/P buffer 0 | S/P buffer 1 | O_0 | O_1 (128 + 128 + 2*D columns).
-// The next score product into a buffer is issued after the P.V product that
-// reads it; tcgen05.mma from one thread execute in issue order.
+// Tensor memory: S/P buffers 0 | 1 | 2 (128 columns each) | O (D columns).
+// Tile j uses buffer j % 3, so the score products of the next two tiles are
+// ready while a group turns S_j into P_j (written over the columns of S_j it
+// has read), and the two groups run consecutive tiles side by side.  Both
+// accumulate into the one O with a running maximum they share through shared
+// memory; the details are at prefill_tc_kernel below.
 //
 // Semantics follow mxflashattn/reference.py:8-85: GQA head h reads KV head
 // h / (HQ/HKV); causal masking is bottom-right aligned; a row that sees no
@@ -219,6 +213,25 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// 16 / 8 consecutive 32-bit columns (the masked softmax path works in
+// 16-column chunks so its code stays small).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
 // Shared-memory matrix descriptor: 128-byte swizzle, descriptor version 1.
 //   K-major operand (rows of 64 elements = 128 B): lbo = 16 B (unused), sbo = 1024 B (8-row group stride)
 //   MN-major operand (128-B rows run along N): lbo = stride between 64-wide N blocks,
@@ -240,32 +253,8 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool b_mn_major)
 
 constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
 constexpr int kTcKeys = 128;   // keys per tile (MMA N of S, K of P.V)
-constexpr int kTcThreads = 384;
 constexpr int kTcGroupWarps = 4;  // warps per softmax group (one per tensor-memory lane quadrant)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when a row max grows by > 2^8
-
-template <int HD>
-struct TcCfg {
-  static constexpr int kDBlk = HD / 64;
-  static constexpr int kStages = 3;
-  static constexpr int kBlk = 128 * 128;               // one 64-column block of a 128-row tile
-  static constexpr int kTile = kDBlk * kBlk;           // Q, K or V tile bytes
-  static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
-  static constexpr int kV = kK + kStages * kTile;
-  static constexpr int kMl = kQ;                       // merge scratch over Q once every product is done
-  static constexpr int kBar = kV + kStages * kTile;
-  static constexpr int kNumBars = 1 + 4 * kStages + 6;
-  static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 512;           // S/P 0 | S/P 1 | O_0 | O_1
-  static constexpr uint32_t kTmemO = 2 * kTcKeys;      // O_g at kTmemO + g * HD
-};
-
-template <int kStages>
-struct TcBars {
-  uint64_t q_full, k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], p_full[2], pv_done[2];
-};
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -283,16 +272,85 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   }
 }
 
+template <int HD>
+struct TcCfg {
+  // softmax groups of 4 warps (one per tensor-memory lane quadrant); group g
+  // takes key tiles j with j % kGroups == g
+  static constexpr int kGroups = 2;  // three groups measured no faster
+  static constexpr int kThreads = (4 + 4 * kGroups) * 32;
+  static constexpr int kDBlk = HD / 64;
+  static constexpr int kStages = 3;
+  static constexpr int kBlk = 128 * 128;               // one 64-column block of a 128-row tile
+  static constexpr int kTile = kDBlk * kBlk;           // Q, K or V tile bytes
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kTile;
+  static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kMl = kQ;                       // epilogue (m, l) exchange over Q once every product is done
+  static constexpr int kMPub = kV + kStages * kTile;   // [2 parities][128 rows] running max handed between groups
+  static constexpr int kBar = kMPub + 2 * kTcRows * 4;
+  static constexpr int kNumBars = 1 + 2 * kStages + 3 * 3 + 2 * 4 + 1;
+  static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 512;           // S/P 0 | S/P 1 | S/P 2 | O
+  static constexpr uint32_t kTmemO = 3 * kTcKeys;
+  static constexpr int kSBufs = 3;
+};
+
+// K stage t%3 is released by S_t's completion (s_full) and V stage t%3 by
+// P.V_t's (pv_done): one commit per product, each barrier read by every
+// party that needs that product done.
+template <int kStages>
+struct TcBars {
+  uint64_t q_full, k_full[kStages], v_full[kStages];
+  uint64_t s_full[3], p_full[3], pv_done[3];
+  uint64_t m_ready[2][4];  // [tile parity][warp quadrant]
+  // Completes once, after the last P.V (and so every product): the epilogue
+  // must not wait on a per-buffer barrier by parity, since a group that ran
+  // out of tiles early can reach it two phases ahead of that barrier.
+  uint64_t all_done;
+};
+
+// One output accumulator, three score buffers.  A layout with an O per
+// softmax group (S0 | S1 | O0 | O1) fills tensor memory and forces the next
+// score product into a buffer after the P.V product that reads the P stored
+// there, so every group tile waits for its own softmax, one P.V and one score
+// product in series.  With one O there is room for three S/P buffers: while a
+// group turns S_j into P_j, S_{j+1} and S_{j+2} are already computed.
+//
+// One O means one running maximum per row for both groups.  The group of
+// tile j reads m_{j-1} (published by the other group through shared memory,
+// one mbarrier per warp quadrant and tile parity), raises it only when the
+// tile's row maximum exceeds it by more than 2^8 (lazy rescale), and
+// publishes m_j before its exp2 pass.  When m_j grew it rescales O in tensor
+// memory after P.V_{j-1} completed and before P.V_j is issued (P.V_j waits
+// for P_j, which this group has not released yet).  Each group keeps its own
+// row sum at the maximum of its last tile; the epilogue brings both to the
+// final maximum, which is also O's.
+//
+// The score and P.V products come from two issuing threads (warps 2 and 1):
+// an issuing thread is held until the tensor pipe accepts each MMA, so one
+// thread's waits and commits between chains left the pipe idle, while with
+// two the other thread's chain fills those gaps.  Each product is committed
+// once: s_full[b] (read by the softmax and by the producer, which then
+// reloads that K stage) and pv_done[b] (read by the score issuer before it
+// reuses buffer b, by the producer before it reloads that V stage, and by a
+// rescaling softmax group).  No barrier is waited on more than one phase
+// ahead of its state; the epilogue, which a group can reach while the last
+// tile's buffer is still two phases behind, waits on a one-shot barrier.
 template <typename T, int HD>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
-                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
+                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
   using Cfg = TcCfg<HD>;
   constexpr int NS = Cfg::kStages;
+  constexpr int NB = Cfg::kSBufs;
+  constexpr int NG = Cfg::kGroups;
+  static_assert(2 * NG * kTcRows * 4 <= Cfg::kTile, "epilogue exchange fits the Q tile");
+  static_assert(Cfg::kTmemO + HD <= Cfg::kTmemCols, "tensor memory layout");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   TcBars<NS>* bars = reinterpret_cast<TcBars<NS>*>(sm + Cfg::kBar);
-  float* ml = reinterpret_cast<float*>(sm + Cfg::kMl);  // [group][m | l][row]
+  float* ml = reinterpret_cast<float*>(sm + Cfg::kMl);      // [group][m | l][row]
+  float* mpub = reinterpret_cast<float*>(sm + Cfg::kMPub);  // [tile parity][row]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kBar + Cfg::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -341,15 +399,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(&bars->q_full, 1);
     for (int i = 0; i < NS; ++i) {
       mbar_init(&bars->k_full[i], 1);
-      mbar_init(&bars->k_empty[i], 1);
       mbar_init(&bars->v_full[i], 1);
-      mbar_init(&bars->v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NB; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], kTcGroupWarps);
       mbar_init(&bars->pv_done[i], 1);
     }
+    for (int i = 0; i < 2; ++i)
+      for (int qd = 0; qd < 4; ++qd) mbar_init(&bars->m_ready[i][qd], 32);
+    mbar_init(&bars->all_done, 1);
     *abort = 0;
     fence_mbar_init();
   }
@@ -372,119 +431,117 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int db = 0; db < Cfg::kDBlk; ++db)
         tma_load_3d(sm + Cfg::kQ + db * Cfg::kBlk, &tmq, &bars->q_full, db * 64, h, q_start + q0);
-      for (int t = 0; t < nkt && !*abort; ++t) {
-        const int st = t % NS, use = t / NS;
-        if (use > 0 && !tc_wait(&bars->k_empty[st], (use - 1) & 1, abort)) break;
-        mbar_arrive_expect_tx(&bars->k_full[st], Cfg::kTile);
+      // Issue order = consumption order: K_0..K_2, then per tile V_t and K_{t+3}.
+      // K_{t+3} replaces K_t once S_t is done; V_t replaces V_{t-3} once P.V_{t-3}
+      // is done.  Neither copy ever waits behind a wait of the other kind that
+      // the tensor pipe reaches later.
+      auto load_k = [&](int t) {
+        mbar_arrive_expect_tx(&bars->k_full[t % NS], Cfg::kTile);
 #pragma unroll
         for (int db = 0; db < Cfg::kDBlk; ++db)
-          tma_load_3d(sm + Cfg::kK + st * Cfg::kTile + db * Cfg::kBlk, &tmk, &bars->k_full[st], db * 64, hk,
-                      k_start + t * kTcKeys);
-        if (use > 0 && !tc_wait(&bars->v_empty[st], (use - 1) & 1, abort)) break;
+          tma_load_3d(sm + Cfg::kK + (t % NS) * Cfg::kTile + db * Cfg::kBlk, &tmk, &bars->k_full[t % NS], db * 64,
+                      hk, k_start + t * kTcKeys);
+      };
+      for (int t = 0; t < NS && t < nkt; ++t) load_k(t);
+      for (int t = 0; t < nkt && !*abort; ++t) {
+        const int st = t % NS, use = t / NS;
+        if (use > 0 && !tc_wait(&bars->pv_done[st], (use - 1) & 1, abort)) break;  // P.V_{t-3} done
         mbar_arrive_expect_tx(&bars->v_full[st], Cfg::kTile);
 #pragma unroll
         for (int db = 0; db < Cfg::kDBlk; ++db)
           tma_load_3d(sm + Cfg::kV + st * Cfg::kTile + db * Cfg::kBlk, &tmv, &bars->v_full[st], db * 64, hk,
                       k_start + t * kTcKeys);
+        if (t + NS < nkt) {
+          if (!tc_wait(&bars->s_full[st], use & 1, abort)) break;  // S_t done with this stage
+          load_k(t + NS);
+        }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     // ------------------------------------------------------------ MMA issue
+    // Two issuing threads: warp 1 issues the P.V products, warp 2 the score
+    // products.  An issuing thread is held until the tensor pipe accepts
+    // each MMA, so with one thread every wait, commit and descriptor step
+    // between two chains left the pipe idle; with two, one thread's chain
+    // keeps the pipe busy while the other waits.  S_{t+3} reuses buffer t%3
+    // only after P.V_t completed (pv_done), and P.V_t reads S_t's buffer only
+    // after the softmax released P_t, which it does after S_t completed.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc<T>(kTcRows, kTcKeys, false);
       constexpr uint32_t idesc_o = umma_idesc<T>(kTcRows, HD, true);
       constexpr int kS = HD / 16;        // K-steps of a score product
       constexpr int kP = kTcKeys / 16;   // K-steps of a P.V product
-      // Descriptor start addresses are in 16-byte units (bits 0-13) and every
-      // operand lies inside shared memory, so a step is a plain add.  Q and K
-      // (K-major) advance 32 bytes per 16-column step within a 128-byte row
-      // and a whole 64-column block every four steps; V (MN-major) advances 16
-      // key rows = 2 KB per step.
-      auto s_step = [](int kk) -> uint64_t { return (kk >> 2) * (Cfg::kBlk >> 4) + (kk & 3) * 2; };
-      uint64_t qd[kS];
-      {
-        const uint64_t base = smem_desc(smem_u32(sm + Cfg::kQ), 16, 1024);
-#pragma unroll
-        for (int kk = 0; kk < kS; ++kk) qd[kk] = base + s_step(kk);
-      }
-      auto k_descs = [&](int st, uint64_t (&kd)[kS]) {
-        const uint64_t base = smem_desc(smem_u32(sm + Cfg::kK + st * Cfg::kTile), 16, 1024);
-#pragma unroll
-        for (int kk = 0; kk < kS; ++kk) kd[kk] = base + s_step(kk);
-      };
-      bool ok = tc_wait(&bars->q_full, 0, abort);
-      for (int t = 0; t < 2 && t < nkt && ok; ++t) {
-        uint64_t kd[kS];
-        k_descs(t % NS, kd);
-        const int st = t % NS;
-        if (!tc_wait(&bars->k_full[st], (t / NS) & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        umma_ss_chain(tmem + t * kTcKeys, qd, kd, idesc_s);
-        umma_commit(&bars->s_full[t]);
-        umma_commit(&bars->k_empty[st]);
-      }
-      for (int j = 0; j < nkt && ok; ++j) {
-        const int pb = j & 1, vs = j % NS, ks = (j + 2) % NS;
-        const bool next_s = j + 2 < nkt;
-        // everything the two products need is computed before the waits
-        uint64_t vd[kP], kd[kS];
-        uint32_t pa[kP];
+      if (warp == 2) {
+        auto s_step = [](int kk) -> uint64_t { return (kk >> 2) * (Cfg::kBlk >> 4) + (kk & 3) * 2; };
+        uint64_t qd[kS];
         {
-          const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
+          const uint64_t base = smem_desc(smem_u32(sm + Cfg::kQ), 16, 1024);
 #pragma unroll
-          for (int kk = 0; kk < kP; ++kk) {
-            vd[kk] = vbase + kk * (16 * 128 >> 4);
-            // 16 keys = 8 packed columns of P_j (written over S_j in buffer j%2)
-            pa[kk] = tmem + pb * kTcKeys + kk * 8;
+          for (int kk = 0; kk < kS; ++kk) qd[kk] = base + s_step(kk);
+        }
+        bool ok = tc_wait(&bars->q_full, 0, abort);
+        for (int t = 0; t < nkt && ok; ++t) {
+          const int buf = t % NB, ks = t % NS;
+          uint64_t kd[kS];
+          {
+            const uint64_t base = smem_desc(smem_u32(sm + Cfg::kK + ks * Cfg::kTile), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kS; ++kk) kd[kk] = base + s_step(kk);
           }
+          pin_regs(kd);
+          if (t >= NB && !tc_wait(&bars->pv_done[buf], ((t - NB) / NB) & 1, abort)) break;  // buffer free
+          if (!tc_wait(&bars->k_full[ks], (t / NS) & 1, abort)) break;
+          tc_fence_after();
+          umma_ss_chain(tmem + buf * kTcKeys, qd, kd, idesc_s);
+          umma_commit(&bars->s_full[buf]);
         }
-        k_descs(ks, kd);
-        pin_regs(vd);
-        pin_regs(kd);
-        pin_regs(pa);
-        // K_{j+2} and V_j landed long before P_j is ready: wait for them
-        // first, so nothing but P_j stands between the softmax and the two
-        // products
-        if (next_s && !tc_wait(&bars->k_full[ks], ((j + 2) / NS) & 1, abort)) break;
-        if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
-        if (!tc_wait(&bars->p_full[pb], (j >> 1) & 1, abort)) break;
-        tc_fence_after();
-        umma_ts_chain(tmem + Cfg::kTmemO + pb * HD, pa, vd, idesc_o, j >= 2 ? 1u : 0u);
-        // S_{j+2} reuses buffer j%2; it is issued after the P.V product above
-        if (next_s) umma_ss_chain(tmem + pb * kTcKeys, qd, kd, idesc_s);
-        // each commit tracks every product issued before it
-        if (next_s) {
-          umma_commit(&bars->s_full[pb]);
-          umma_commit(&bars->k_empty[ks]);
+      } else {
+        for (int j = 0; j < nkt; ++j) {
+          const int buf = j % NB, vs = j % NS;
+          uint64_t vd[kP];
+          uint32_t pa[kP];
+          {
+            const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kP; ++kk) {
+              vd[kk] = vbase + kk * (16 * 128 >> 4);
+              pa[kk] = tmem + buf * kTcKeys + kk * 8;  // P_j packed over the columns of S_j
+            }
+          }
+          pin_regs(vd);
+          pin_regs(pa);
+          if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
+          if (!tc_wait(&bars->p_full[buf], (j / NB) & 1, abort)) break;
+          tc_fence_after();
+          umma_ts_chain(tmem + Cfg::kTmemO, pa, vd, idesc_o, j > 0 ? 1u : 0u);
+          umma_commit(&bars->pv_done[buf]);
+          // every score product completed before P_{nkt-1} existed, so this
+          // marks the end of all tensor-memory and shared-memory reads
+          if (j == nkt - 1) umma_commit(&bars->all_done);
         }
-        umma_commit(&bars->pv_done[pb]);
-        umma_commit(&bars->v_empty[vs]);
       }
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
-    const int g = (warp - 4) >> 2;          // group: key tiles j with j % 2 == g
+    const int g = (warp - 4) >> 2;          // group: key tiles j with j % NG == g
     const int quad = warp & 3;              // tensor-memory lane quadrant
     const int r = quad * 32 + lane;         // query row within the tile == tensor-memory lane
     const int qi = q0 + r;                  // query index within the sequence
     const uint32_t lane_base = tmem + ((static_cast<uint32_t>(quad) * 32u) << 16);
-    const uint32_t o_base = lane_base + Cfg::kTmemO + g * HD;
+    const uint32_t o_base = lane_base + Cfg::kTmemO;
     const int vis_end = p.causal ? min(k_len, qi + shift + 1) : k_len;  // keys [0, vis_end) visible
     const float sc = p.scale_log2;
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_own = -INFINITY, l_own = 0.f;   // this group's row sum, at the maximum of its last tile
     bool ok = true;
-    for (int j = g; j < nkt; j += 2) {
-      // wait results are made warp-uniform: tcgen05.ld/st are warp-collective
-      if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[g], (j >> 1) & 1, abort))) {
+    for (int j = g; j < nkt; j += NG) {
+      const int buf = j % NB;
+      if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[buf], (j / NB) & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sbuf = lane_base + g * kTcKeys;
+      const uint32_t sbuf = lane_base + buf * kTcKeys;
       const int key0 = j * kTcKeys;
       const bool full = key0 + kTcKeys <= vis_end;
 
@@ -492,22 +549,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // positive scale, min for a negative one), scaled into the log2 domain
       const bool all_full = __all_sync(0xffffffffu, full);
       const bool pos = sc >= 0.f;
-      float ext = pos ? -INFINITY : INFINITY;
+      const float ext0 = pos ? -INFINITY : INFINITY;
+      float ext = ext0;
+      if (all_full) {
+        // four independent chains, so the compare latency overlaps
+        float e0 = ext0, e1 = ext0, e2 = ext0, e3 = ext0;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 64) {
+          uint32_t raw[64];
+          tmem_ld64(sbuf + c, raw);
 #pragma unroll
-      for (int c = 0; c < kTcKeys; c += 64) {
-        uint32_t raw[64];
-        tmem_ld64(sbuf + c, raw);
-        if (all_full) {
-          float e0 = ext, e1 = pos ? -INFINITY : INFINITY;
-#pragma unroll
-          for (int i = 0; i < 64; i += 2) {
+          for (int i = 0; i < 64; i += 4) {
             e0 = pos ? fmaxf(e0, __uint_as_float(raw[i])) : fminf(e0, __uint_as_float(raw[i]));
             e1 = pos ? fmaxf(e1, __uint_as_float(raw[i + 1])) : fminf(e1, __uint_as_float(raw[i + 1]));
+            e2 = pos ? fmaxf(e2, __uint_as_float(raw[i + 2])) : fminf(e2, __uint_as_float(raw[i + 2]));
+            e3 = pos ? fmaxf(e3, __uint_as_float(raw[i + 3])) : fminf(e3, __uint_as_float(raw[i + 3]));
           }
-          ext = pos ? fmaxf(e0, e1) : fminf(e0, e1);
-        } else {
+        }
+        ext = pos ? fmaxf(fmaxf(e0, e1), fmaxf(e2, e3)) : fminf(fminf(e0, e1), fminf(e2, e3));
+      } else {
+        // diagonal tile: a rolled loop over 16-column chunks keeps this
+        // rarely taken path out of the way of the unrolled one
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
+          for (int i = 0; i < 16; ++i) {
             const float v = __uint_as_float(raw[i]);
             const bool vis = key0 + c + i < vis_end;
             ext = vis ? (pos ? fmaxf(ext, v) : fminf(ext, v)) : ext;
@@ -515,16 +583,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       const float mx = (ext == INFINITY || ext == -INFINITY) ? -INFINITY : ext * sc;
-      const bool grow = mx > m_run + kRescaleThreshold;
-      float alpha = 1.f;
-      if (grow) {
-        alpha = fast_exp2(m_run - mx);  // 0 when m_run = -inf
-        m_run = mx;
-        l_run *= alpha;
+
+      // the running maximum after tile j-1, from the other group
+      float m_in = -INFINITY;
+      if (j > 0) {
+        const int pj = j - 1;
+        if (!__all_sync(0xffffffffu, tc_wait(&bars->m_ready[pj & 1][quad], (pj >> 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        m_in = mpub[(pj & 1) * kTcRows + r];
       }
-      // O_g last received P.V of tile j-2, which completed before S_j (same
-      // issuing thread), so it is at rest here; rescale it when a row max grew
-      if (__any_sync(0xffffffffu, grow) && j >= 2) {
+      const float m_j = mx > m_in + kRescaleThreshold ? mx : m_in;
+      // every lane releases its own row's value (arrival count 32)
+      mpub[(j & 1) * kTcRows + r] = m_j;
+      mbar_arrive(&bars->m_ready[j & 1][quad]);
+
+      if (m_j != m_own) {  // this group's sum follows the maximum it now uses
+        l_own *= fast_exp2(m_own - m_j);  // 0 when m_own = -inf
+        m_own = m_j;
+      }
+      // O holds tiles < j at m_in; bring it to m_j once P.V_{j-1} is done
+      // (P.V_j cannot start before this group releases P_j)
+      const bool grow = j > 0 && m_j != m_in;
+      if (__any_sync(0xffffffffu, grow)) {
+        const int pj = j - 1;
+        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv_done[pj % NB], (pj / NB) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float alpha = grow ? fast_exp2(m_in - m_j) : 1.f;  // 0 when m_in = -inf
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t o[32];
@@ -535,30 +624,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
 
-      // pass 2: P = 2^(s*scale - m) over each 64-key half, packed in pairs into
-      // the 32 columns of S that the halves before it already consumed
+      // pass 2: P = 2^(s*scale - m_j) over each 64-key half, packed in pairs
+      // into the 32 columns of S that the halves before it already consumed
       float rs = 0.f;
-      const float neg_m = -m_run;
-      const bool live = m_run != -INFINITY;
+      const float neg_m = -m_j;
+      if (all_full) {  // every row sees every key of the tile, so m_j is finite
+        float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 64) {
+          uint32_t raw[64];
+          tmem_ld64(sbuf + c, raw);
+          uint32_t packed[32];
 #pragma unroll
-      for (int c = 0; c < kTcKeys; c += 64) {
-        uint32_t raw[64];
-        tmem_ld64(sbuf + c, raw);
-        uint32_t packed[32];
-        if (all_full && live) {
-          float r0 = 0.f, r1 = 0.f;
-#pragma unroll
-          for (int i = 0; i < 64; i += 2) {
+          for (int i = 0; i < 64; i += 4) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m));
             const float p1 = fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m));
+            const float p2 = fast_exp2(fmaf(__uint_as_float(raw[i + 2]), sc, neg_m));
+            const float p3 = fast_exp2(fmaf(__uint_as_float(raw[i + 3]), sc, neg_m));
             r0 += p0;
             r1 += p1;
+            r2 += p2;
+            r3 += p3;
             packed[i >> 1] = Elem<T>::pack(p0, p1);
+            packed[(i >> 1) + 1] = Elem<T>::pack(p2, p3);
           }
-          rs += r0 + r1;
-        } else {
+          tmem_st32(sbuf + (c >> 1), packed);
+        }
+        rs = (r0 + r1) + (r2 + r3);
+      } else {
+        const bool live = m_j != -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
+          uint32_t packed[8];
 #pragma unroll
-          for (int i = 0; i < 64; i += 2) {
+          for (int i = 0; i < 16; i += 2) {
             const bool v0 = live && key0 + c + i < vis_end;
             const bool v1 = live && key0 + c + i + 1 < vis_end;
             const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
@@ -566,63 +667,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             rs += p0 + p1;
             packed[i >> 1] = Elem<T>::pack(p0, p1);
           }
+          // P columns [c/2, c/2 + 8) lie in the S columns already read
+          tmem_st8(sbuf + (c >> 1), packed);
         }
-        tmem_st32(sbuf + (c >> 1), packed);
       }
-      l_run += rs;
+      l_own += rs;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[g]);
+      if (lane == 0) mbar_arrive(&bars->p_full[buf]);
     }
 
     // ---------------------------------------------------------- merge + store
-    // Both accumulators must be complete; the last P.V is the last product,
-    // so afterwards the Q tile's shared memory is free for the (m, l) exchange.
-    bool done_ok = ok;
-#pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-      if (nkt > gg) {
-        const int jl = gg + ((nkt - 1 - gg) >> 1) * 2;  // last tile of parity gg
-        done_ok = __all_sync(0xffffffffu, done_ok && tc_wait(&bars->pv_done[gg], (jl >> 1) & 1, abort));
-      }
-    }
+    // Every product is complete once the last P.V is; the Q tile's shared
+    // memory is then free for the (m, l) exchange.
+    const bool done_ok = __all_sync(0xffffffffu, ok && tc_wait(&bars->all_done, 0, abort));
     fence_proxy_async_smem();
-    ml[(g * 2) * kTcRows + r] = m_run;
-    ml[(g * 2 + 1) * kTcRows + r] = l_run;
-    named_barrier_sync(1, 2 * kTcGroupWarps * 32);
+    ml[(g * 2) * kTcRows + r] = m_own;
+    ml[(g * 2 + 1) * kTcRows + r] = l_own;
+    named_barrier_sync(1, NG * kTcGroupWarps * 32);
     if (done_ok) {
       tc_fence_after();
-      const float m0 = ml[r], l0 = ml[kTcRows + r];
-      const float m1 = ml[2 * kTcRows + r], l1 = ml[3 * kTcRows + r];
-      const float M = fmaxf(m0, m1);
-      const float a0 = m0 != -INFINITY ? fast_exp2(m0 - M) : 0.f;
-      const float a1 = m1 != -INFINITY ? fast_exp2(m1 - M) : 0.f;
-      const float L = l0 * a0 + l1 * a1;
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      const float w0 = a0 * inv, w1 = a1 * inv;
-      const bool two = nkt > 1;
-      T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
-      // group g stores columns [g*HD/2, (g+1)*HD/2)
+      float M = -INFINITY;  // the last tile's maximum, at which O is held
 #pragma unroll
-      for (int c = g * (HD / 2); c < (g + 1) * (HD / 2); c += 32) {
-        uint32_t o0[32], o1[32];
-        tmem_ld32(lane_base + Cfg::kTmemO + c, o0);
-        if (two) tmem_ld32(lane_base + Cfg::kTmemO + HD + c, o1);
+      for (int gg = 0; gg < NG; ++gg) M = fmaxf(M, ml[(gg * 2) * kTcRows + r]);
+      float L = 0.f;
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        const float mg = ml[(gg * 2) * kTcRows + r];
+        if (mg != -INFINITY) L += ml[(gg * 2 + 1) * kTcRows + r] * fast_exp2(mg - M);
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
+      // group g stores the 32-column chunks g, g + NG, ...
+      for (int c = g * 32; c < HD; c += NG * 32) {
+        uint32_t o[32];
+        tmem_ld32(o_base + c, o);
         if (qi < q_len) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x0 = w0 > 0.f ? __uint_as_float(o0[i + e]) * w0 : 0.f;
-              const float x1 = (two && w1 > 0.f) ? __uint_as_float(o1[i + e]) * w1 : 0.f;
-              f[e] = x0 + x1;
-            }
             uint4 v;
-            v.x = Elem<T>::pack(f[0], f[1]);
-            v.y = Elem<T>::pack(f[2], f[3]);
-            v.z = Elem<T>::pack(f[4], f[5]);
-            v.w = Elem<T>::pack(f[6], f[7]);
+            v.x = Elem<T>::pack(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+            v.y = Elem<T>::pack(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            v.z = Elem<T>::pack(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+            v.w = Elem<T>::pack(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + c + i) = v;
           }
         }

@@ -89,12 +89,19 @@ def shadow_summary(path: Path | None) -> dict | None:
     checks = [c for c in checks if c.get("path") == "shadow_check"]
     if not checks:
         return None
-    return {
+    summary = {
         "checks": len(checks),
         "max_abs_diff": max(c["max_abs_diff"] for c in checks),
         "max_abs_ref": max(c["max_abs_ref"] for c in checks),
         "worst_relative": max(c["max_abs_diff"] / max(c["max_abs_ref"], 1e-30) for c in checks),
     }
+    exact = [c for c in checks if "max_ulps_kernel_vs_fp32" in c]
+    if exact:
+        summary["fp32_checks"] = len(exact)
+        summary["max_ulps_kernel_vs_fp32"] = max(c["max_ulps_kernel_vs_fp32"] for c in exact)
+        summary["max_ulps_vllm_vs_fp32"] = max(c["max_ulps_vllm_vs_fp32"] for c in exact)
+        summary["max_abs_fp32"] = max(c["max_abs_fp32"] for c in exact)
+    return summary
 
 
 def compare_runs(baseline: dict, candidate: dict) -> dict:
@@ -158,7 +165,7 @@ def run(args) -> dict:
         model = str(write_model_dir(model, tempfile.mkdtemp(prefix="mxfa_vllm_")))
     engine = LLM(model=model, load_format="dummy", skip_tokenizer_init=True, enforce_eager=args.eager,
                  max_model_len=args.max_model_len, gpu_memory_utilization=args.gpu_memory_utilization,
-                 seed=args.seed, dtype="bfloat16", attention_backend="FLASH_ATTN")
+                 seed=args.seed, dtype=args.dtype, attention_backend="FLASH_ATTN")
     prompts = make_prompts(args.batch, args.prompt_min, args.prompt_max, args.seed)
     params = SamplingParams(temperature=0.0, max_tokens=args.max_tokens, ignore_eos=True, detokenize=False,
                             logprobs=0)
@@ -193,6 +200,7 @@ def run(args) -> dict:
         "torch": torch.__version__,
         "device": torch.cuda.get_device_name(),
         "batch": args.batch,
+        "dtype": args.dtype,
         "prompt_lengths": [args.prompt_min, args.prompt_max],
         "max_tokens": args.max_tokens,
         "eager": args.eager,
@@ -224,6 +232,7 @@ def main() -> None:
     parser.add_argument("--max-model-len", type=int, default=2048)
     parser.add_argument("--gpu-memory-utilization", type=float, default=0.5)
     parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--dtype", choices=("bfloat16", "float16"), default="bfloat16")
     parser.add_argument("--graphs", dest="eager", action="store_false", help="let vLLM compile and capture graphs")
     parser.add_argument("--output", type=Path, default=Path("vllm-run.json"))
     parser.add_argument("--event-sample", type=int, default=64, help="record one dispatch event per N calls")

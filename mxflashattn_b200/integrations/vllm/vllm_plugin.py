@@ -284,12 +284,54 @@ def _shadow_check(impl, layer, query, key, value, kv_cache, attn_metadata, outpu
     n = result.shape[0]
     mine = result.reshape(n, -1).float()
     theirs = ref[:n].reshape(n, -1).float()
-    _record_worker_event({
+    event = {
         "path": "shadow_check",
         "tokens": int(n),
         "max_abs_diff": float((mine - theirs).abs().max()),
         "max_abs_ref": float(theirs.abs().max()),
-    })
+    }
+    exact = _fp32_decode_reference(query, kv_cache, attn_metadata, impl.scale, n)
+    if exact is not None:
+        # scale-free: each element's error in units of one bf16 ulp of the exact value
+        event["max_ulps_kernel_vs_fp32"] = _max_ulps(mine, exact)
+        event["max_ulps_vllm_vs_fp32"] = _max_ulps(theirs, exact)
+        event["max_abs_fp32"] = float(exact.abs().max())
+    _record_worker_event(event)
+
+
+def _fp32_decode_reference(query, kv_cache, attn_metadata, scale, n):
+    """fp32 attention of the n live decode queries over their cached keys
+    (gathered through the block table), the math of mxflashattn/reference.py
+    in torch: softmax(q k^T * scale) v per sequence, GQA heads sharing a KV
+    head.  None when the metadata is not one query token per sequence."""
+    import torch
+
+    seq_lens = attn_metadata.seq_lens.reshape(-1)
+    if seq_lens.numel() != n or int(getattr(attn_metadata, "max_query_len", 1)) != 1:
+        return None
+    key_cache, value_cache = kv_cache.unbind(0)
+    page, hkv, d = key_cache.shape[1], key_cache.shape[2], key_cache.shape[3]
+    hq = query.shape[1]
+    out = torch.empty((n, hq, d), device=query.device, dtype=torch.float32)
+    lens = seq_lens.tolist()
+    table = attn_metadata.block_table
+    for b, length in enumerate(lens):
+        pages = table[b, : (int(length) + page - 1) // page].long()
+        k = key_cache[pages].reshape(-1, hkv, d)[: int(length)].float()
+        v = value_cache[pages].reshape(-1, hkv, d)[: int(length)].float()
+        q = query[b].float().reshape(hkv, hq // hkv, d)
+        s = torch.einsum("hgd,thd->hgt", q, k) * scale
+        out[b] = torch.einsum("hgt,thd->hgd", torch.softmax(s, dim=-1), v).reshape(hq, d)
+    return out.reshape(n, -1)
+
+
+def _max_ulps(actual, exact) -> float:
+    """max |actual - exact| / ulp_bf16(exact), with the ulp floored at the smallest normal bf16 ulp."""
+    import torch
+
+    mag = exact.abs().clamp_min(2.0 ** -126)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+    return float(((actual - exact).abs() / ulp).max())
 
 
 class MXFlashAttnBackend(FlashAttentionBackend):
