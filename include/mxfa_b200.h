@@ -218,9 +218,12 @@ int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int 
  * minus the workspace: the split partials go to one buffer of
  * MXFA_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that
  * loads the library holds until the process exits.  Calls needing more
- * scratch than that fail with MXFA_ERR_UNSUPPORTED and a message.  The
+ * scratch than that fail with MXFA_ERR_UNSUPPORTED and a message (argument
+ * errors are reported first, as by mxfa_kvcache_attention_launch).  The
  * first call on a device looks up the buffer's device address with that
- * device current (make that first call before any stream capture).  All
+ * device current (make that first call before any stream capture); a call
+ * made after the device's context was re-created, as by cudaDeviceReset,
+ * looks it up again.  All
  * calls on a device share the one buffer, so calls that overlap on the GPU
  * (other streams, other host threads) race and must be serialised by the
  * caller.  Nothing is allocated or freed by this call. */
