@@ -339,6 +339,24 @@ __device__ __noinline__ void merge_split_row_publish_call(const float* ows, cons
   merge_split_row_publish<HD>(ows, mdws, r, NP, lane, bufs, world, rank, rows, rec_off);
 }
 
+// e4m3 tiles: token order of the score product.  ldmatrix .m16n16 .trans
+// .b8 hands lane (g, t4) the bytes of tokens 4*t4 .. 4*t4+3 for head-dim
+// rows g and g+8, so after widening, K-step slots (2*t4, 2*t4+1) of the f16
+// P.V product hold tokens (4*t4, 4*t4+1) and slots (2*t4+8, 2*t4+9) tokens
+// (4*t4+2, 4*t4+3).  The score product's M rows are loaded in the same
+// order (row i is token fp8_tok(i)), so P arrives with its K slots already
+// matching V and no register transpose of V is needed.
+__device__ __forceinline__ int fp8_tok(int i) { return 4 * ((i & 7) >> 1) + (i & 1) + ((i >> 3) << 1); }
+
+// Two 16x16 byte tiles transposed: lanes 0-15 give the 16 rows of the first,
+// lanes 16-31 those of the second.
+__device__ __forceinline__ void ldsm_b8_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                 uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
 __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPerSm)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
@@ -683,9 +701,10 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) s2[nt][0] = s2[nt][1] = s2[nt][2] = s2[nt][3] = 0.f;
       // one ldmatrix.x4 = two 16-column steps x two 8-token halves of fp8 K;
-      // each register (4 e4m3 values) becomes the step's low and high f16x2
+      // each register (4 e4m3 values) becomes the step's low and high f16x2;
+      // M row i of the product is token fp8_tok(i)
       const int q8 = lane >> 3;
-      const int r = ((q8 & 1) << 3) + (lane & 7);
+      const int r = fp8_tok(((q8 & 1) << 3) + (lane & 7));
 #pragma unroll
       for (int c2 = 0; c2 < HD / 32; ++c2) {
         uint32_t x[4];
@@ -731,7 +750,8 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int pos = pos0 + g + ((e >> 1) << 3);
+          const int row = g + ((e >> 1) << 3);  // M row of the score product
+          const int pos = pos0 + (kFp8 ? fp8_tok(row) : row);
           const bool ok = pos >= lo && pos < hi && pos <= lim[nt][e & 1];
           s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
         }
@@ -796,31 +816,25 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
         pl[nt][hh] = movmatrix_trans(Elem<MT>::pack(a - hf.x, c - hf.y));
       }
     if constexpr (kFp8) {
-      // fp8 V rows are loaded untransposed (same addressing as K), widened to
-      // f16 and transposed in registers: the low and high f16x2 of a register
-      // give O^T rows {4j, 4j+1} and {4j+2, 4j+3} of the 16-column step, so
-      // accumulator row g of step mi holds D column 16*mi + 4*(g/2) + g%2 and
-      // row g+8 holds that column + 2 (undone when the warps merge)
-      const int q8 = lane >> 3;
-      const int r = ((q8 & 1) << 3) + (lane & 7);
+      // fp8 V through the transposing 8-bit ldmatrix: for head-dim step mi,
+      // lane (g, t4) gets V[tokens 4*t4..4*t4+3][d = 16*mi + g] and [.. + 8];
+      // widened, these are the A fragment of V^T with the token order of P
+      // (see fp8_tok), so the accumulator keeps the natural D order
+      const int vrow = lane & 15;  // token row this lane addresses
 #pragma unroll
-      for (int c2 = 0; c2 < HD / 32; ++c2) {
-        uint32_t y[4];
-        ldsm_x4(vbase + swz128(r, 2 * c2 + (q8 >> 1)), y[0], y[1], y[2], y[3]);
+      for (int mi = 0; mi < HD / 16; mi += 2) {
+        uint32_t y0, y1, y2, y3;
+        ldsm_b8_x2_trans(vbase + swz128(vrow, mi + (lane >> 4)), y0, y1, y2, y3);
+        const uint32_t yy[2][2] = {{y0, y1}, {y2, y3}};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int mi = 2 * c2 + h;
-          uint32_t l0, h0, l1, h1;
-          e4m3x4_to_f16x2x2(y[2 * h], l0, h0);
-          e4m3x4_to_f16x2x2(y[2 * h + 1], l1, h1);
-          const uint32_t a0 = movmatrix_trans(l0);
-          const uint32_t a1 = movmatrix_trans(h0);
-          const uint32_t a2 = movmatrix_trans(l1);
-          const uint32_t a3 = movmatrix_trans(h1);
+          uint32_t a0, a2, a1, a3;
+          e4m3x4_to_f16x2x2(yy[h][0], a0, a2);  // d = 16*(mi+h) + g: token slots 2*t4.. and 2*t4+8..
+          e4m3x4_to_f16x2x2(yy[h][1], a1, a3);  // d = 16*(mi+h) + g + 8
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-            Elem<MT>::mma(o[mi][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+            Elem<MT>::mma(o[mi + h][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+            Elem<MT>::mma(o[mi + h][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
           }
         }
       }
@@ -867,7 +881,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int col = nt * 8 + 2 * t4 + (e & 1);
-        const int d = kFp8 ? mi * 16 + 4 * (g >> 1) + (g & 1) + ((e >> 1) << 1) : mi * 16 + g + ((e >> 1) << 3);
+        const int d = mi * 16 + g + ((e >> 1) << 3);
         om[(warp * Mg::kCols + col) * Mg::kStride + d] = kFp8 ? o[mi][nt][e] * p.v_scale : o[mi][nt][e];
       }
   if (g == 0) {
