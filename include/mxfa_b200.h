@@ -299,6 +299,19 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
                            int total_q, int total_k, int HQ, int HKV, int D, int causal, int bf16,
                            float scale, void* stream);
 
+/* mxfa_varlen_fwd_launch with P kept at ~16 significant bits in the P.V
+ * product: P is split into its value rounded to the input type and the
+ * rounded remainder, and both are multiplied with V (1.5x the tensor work).
+ * The default entry rounds P once to the input type, as FlashAttention
+ * does; its error is at most u * (softmax-weighted mean of |V|), u = 2^-9
+ * (bf16) or 2^-11 (fp16), which matters only when V has a wide dynamic
+ * range.  No reference counterpart: the reference's fp32 CPU path
+ * (reference.py:60-85) never rounds P. */
+int mxfa_varlen_fwd_exact_launch(const void* q, const void* k, const void* v, const int32_t* cu_q,
+                                 const int32_t* cu_k, void* out, float* lse, int B, int max_q, int max_k,
+                                 int total_q, int total_k, int HQ, int HKV, int D, int causal, int bf16,
+                                 float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,8 @@ SIGNATURES = {
     "mxfa_seqlens_add_launch": (_i, [_vp, _i, _i, _i, _vp]),
     "mxfa_varlen_fwd_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+    "mxfa_varlen_fwd_exact_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
 }
 
 _lock = threading.Lock()

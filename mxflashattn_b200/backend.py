@@ -91,34 +91,41 @@ def _stream(t: torch.Tensor) -> int:
 # ------------------------------------------------------------------ prefill
 
 def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
-                           softmax_scale, *, return_lse: bool = False):
-    """Packed varlen forward: q [Tq, HQ, D], k/v [Tk, HKV, D] -> out [Tq, HQ, D]."""
+                           softmax_scale, *, return_lse: bool = False, exact_p: bool = False):
+    """Packed varlen forward: q [Tq, HQ, D], k/v [Tk, HKV, D] -> out [Tq, HQ, D].
+
+    ``exact_p``: keep P at ~16 significant bits in the P.V product
+    (``mxfa_varlen_fwd_exact_launch``, 1.5x the tensor work) instead of
+    rounding it once to the input type.
+    """
     q, k, v = _contig(q), _contig(k), _contig(v)
     out = torch.empty_like(q)
     lse = torch.empty((q.shape[0], q.shape[1]), device=q.device, dtype=torch.float32) if return_lse else None
     cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
     batch = cu_q.numel() - 1
+    name = "mxfa_varlen_fwd_exact_launch" if exact_p else "mxfa_varlen_fwd_launch"
     with _on(q):
-        rc = _L().mxfa_varlen_fwd_launch(
+        rc = getattr(_L(), name)(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_q.data_ptr(), cu_k.data_ptr(), out.data_ptr(),
             _lib.ptr(lse), batch, int(max_seqlen_q), int(max_seqlen_k), q.shape[0], k.shape[0], q.shape[1],
             k.shape[1], q.shape[2], int(bool(causal)), _bf16(q), float(softmax_scale), _stream(q))
-    _lib.check(rc, "mxfa_varlen_fwd_launch")
+    _lib.check(rc, name)
     return (out, lse) if return_lse else out
 
 
-def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False):
+def flash_attn_func(q, k, v, causal, softmax_scale, *, return_lse: bool = False, exact_p: bool = False):
     """Dense batched forward: q [B, Sq, HQ, D], k/v [B, Sk, HKV, D] -> out [B, Sq, HQ, D]."""
     q, k, v = _contig(q), _contig(k), _contig(v)
     out = torch.empty_like(q)
     B, Sq, HQ, D = q.shape
     lse = torch.empty((B, Sq, HQ), device=q.device, dtype=torch.float32) if return_lse else None
+    name = "mxfa_varlen_fwd_exact_launch" if exact_p else "mxfa_varlen_fwd_launch"
     with _on(q):
-        rc = _L().mxfa_varlen_fwd_launch(
+        rc = getattr(_L(), name)(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), None, None, out.data_ptr(), _lib.ptr(lse), B, Sq,
             k.shape[1], B * Sq, B * k.shape[1], HQ, k.shape[2], D, int(bool(causal)), _bf16(q),
             float(softmax_scale), _stream(q))
-    _lib.check(rc, "mxfa_varlen_fwd_launch")
+    _lib.check(rc, name)
     return (out, lse) if return_lse else out
 
 

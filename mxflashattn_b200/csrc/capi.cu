@@ -855,9 +855,9 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
   return check_launch("seqlens_add_kernel");
 }
 
-int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+static int varlen_fwd_impl(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
                            void* out, float* lse, int B, int max_q, int max_k, int total_q, int total_k, int HQ,
-                           int HKV, int D, int causal, int bf16, float scale, void* stream) {
+                           int HKV, int D, int causal, int bf16, float scale, void* stream, bool exact) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || max_q < 0 || max_k < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad varlen geometry");
@@ -898,13 +898,36 @@ int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const in
     kern<<<grid, threads, smem, st>>>(p, mq, mk, mv);
     return check_launch("prefill_tc_kernel");
   };
-  static std::atomic<unsigned long long> d0{0}, d1{0}, d2{0}, d3{0};
+  static std::atomic<unsigned long long> d0{0}, d1{0}, d2{0}, d3{0}, e0{0}, e1{0}, e2{0}, e3{0};
+  if (exact) {
+    if (bf16)
+      return D == 128
+                 ? go(prefill_tc_kernel<__nv_bfloat16, 128, true>, TcCfg<128>::kSmemBytes, e0, TcCfg<128>::kThreads)
+                 : go(prefill_tc_kernel<__nv_bfloat16, 64, true>, TcCfg<64>::kSmemBytes, e1, TcCfg<64>::kThreads);
+    return D == 128 ? go(prefill_tc_kernel<__half, 128, true>, TcCfg<128>::kSmemBytes, e2, TcCfg<128>::kThreads)
+                    : go(prefill_tc_kernel<__half, 64, true>, TcCfg<64>::kSmemBytes, e3, TcCfg<64>::kThreads);
+  }
   if (bf16)
     return D == 128 ? go(prefill_tc_kernel<__nv_bfloat16, 128>, TcCfg<128>::kSmemBytes, d0, TcCfg<128>::kThreads)
                     : go(prefill_tc_kernel<__nv_bfloat16, 64>, TcCfg<64>::kSmemBytes, d1, TcCfg<64>::kThreads);
   return D == 128 ? go(prefill_tc_kernel<__half, 128>, TcCfg<128>::kSmemBytes, d2, TcCfg<128>::kThreads)
                   : go(prefill_tc_kernel<__half, 64>, TcCfg<64>::kSmemBytes, d3, TcCfg<64>::kThreads);
 }
+
+int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                           void* out, float* lse, int B, int max_q, int max_k, int total_q, int total_k, int HQ,
+                           int HKV, int D, int causal, int bf16, float scale, void* stream) {
+  return varlen_fwd_impl(q, k, v, cu_q, cu_k, out, lse, B, max_q, max_k, total_q, total_k, HQ, HKV, D, causal, bf16,
+                         scale, stream, false);
+}
+
+int mxfa_varlen_fwd_exact_launch(const void* q, const void* k, const void* v, const int32_t* cu_q,
+                                 const int32_t* cu_k, void* out, float* lse, int B, int max_q, int max_k, int total_q,
+                                 int total_k, int HQ, int HKV, int D, int causal, int bf16, float scale, void* stream) {
+  return varlen_fwd_impl(q, k, v, cu_q, cu_k, out, lse, B, max_q, max_k, total_q, total_k, HQ, HKV, D, causal, bf16,
+                         scale, stream, true);
+}
+
 
 }  // extern "C"
 

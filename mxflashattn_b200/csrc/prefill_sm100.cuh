@@ -336,7 +336,12 @@ struct TcBars {
 // rescaling softmax group).  No barrier is waited on more than one phase
 // ahead of its state; the epilogue, which a group can reach while the last
 // tile's buffer is still two phases behind, waits on a one-shot barrier.
-template <typename T, int HD>
+// kExactP: P is split into its rounded value and the rounded remainder,
+// P_hi + P_lo (~16 significant bits), stored side by side in S's columns
+// (per 16-key chunk: 8 columns of P_hi, then 8 of P_lo) and both multiplied
+// with V, so P.V loses no precision to rounding P.  1.5x the tensor work;
+// for inputs whose V has a wide dynamic range.
+template <typename T, int HD, bool kExactP = false>
 __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
                        const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
@@ -499,13 +504,16 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
         for (int j = 0; j < nkt; ++j) {
           const int buf = j % NB, vs = j % NS;
           uint64_t vd[kP];
-          uint32_t pa[kP];
+          uint32_t pa[kP], pl[kP];
           {
             const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
 #pragma unroll
             for (int kk = 0; kk < kP; ++kk) {
               vd[kk] = vbase + kk * (16 * 128 >> 4);
-              pa[kk] = tmem + buf * kTcKeys + kk * 8;  // P_j packed over the columns of S_j
+              // P_j packed over the columns of S_j: 8 columns per 16 keys, or
+              // (exact P) P_hi then P_lo in the 16 columns of each 16 keys
+              pa[kk] = tmem + buf * kTcKeys + (kExactP ? kk * 16 : kk * 8);
+              pl[kk] = pa[kk] + 8;
             }
           }
           pin_regs(vd);
@@ -514,6 +522,7 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
           if (!tc_wait(&bars->p_full[buf], (j / NB) & 1, abort)) break;
           tc_fence_after();
           umma_ts_chain(tmem + Cfg::kTmemO, pa, vd, idesc_o, j > 0 ? 1u : 0u);
+          if constexpr (kExactP) umma_ts_chain(tmem + Cfg::kTmemO, pl, vd, idesc_o, 1u);
           umma_commit(&bars->pv_done[buf]);
           // every score product completed before P_{nkt-1} existed, so this
           // marks the end of all tensor-memory and shared-memory reads
@@ -628,7 +637,56 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
       // into the 32 columns of S that the halves before it already consumed
       float rs = 0.f;
       const float neg_m = -m_j;
-      if (all_full) {  // every row sees every key of the tile, so m_j is finite
+      if (kExactP && all_full) {
+        // 64-key halves read at once; per 16-key chunk, P_hi then P_lo in the
+        // chunk's own (already read) columns, stored 32 columns at a time
+        float r0 = 0.f, r1 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 64) {
+          uint32_t raw[64];
+          tmem_ld64(sbuf + c, raw);
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            uint32_t packed[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i]), sc, neg_m));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i + 1]), sc, neg_m));
+              r0 += p0;
+              r1 += p1;
+              const uint32_t hi = Elem<T>::pack(p0, p1);
+              const float2 hf = Elem<T>::unpack(hi);
+              const int w = (i >> 4) * 16 + ((i & 15) >> 1);  // chunk i/16: hi words 0-7, lo words 8-15
+              packed[w] = hi;
+              packed[w + 8] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
+            }
+            tmem_st32(sbuf + c + 32 * qq, packed);
+          }
+        }
+        rs = r0 + r1;
+      } else if constexpr (kExactP) {
+        // diagonal tile, 16-key chunks: P_hi and P_lo land in the chunk's own (already read) columns
+        const bool live = m_j != -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const bool v0 = live && (all_full || key0 + c + i < vis_end);
+            const bool v1 = live && (all_full || key0 + c + i + 1 < vis_end);
+            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
+            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
+            rs += p0 + p1;
+            const uint32_t hi = Elem<T>::pack(p0, p1);
+            const float2 hf = Elem<T>::unpack(hi);
+            packed[i >> 1] = hi;
+            packed[8 + (i >> 1)] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
+          }
+          tmem_st16(sbuf + c, packed);
+        }
+      } else if (all_full) {  // every row sees every key of the tile, so m_j is finite
         float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
 #pragma unroll 1
         for (int c = 0; c < kTcKeys; c += 64) {

@@ -55,6 +55,38 @@ def test_varlen_normal_inputs_within_north_star_bound_without_allowance(dt, d, c
     assert_close_out(host(out), ref, dt, f"N(0,1) {dt} d{d} (strict)")
 
 
+@pytest.mark.parametrize("name", sorted(VARLEN_GOLDEN))
+def test_exact_p_varlen_goldens_within_north_star_bound_without_allowance(name, golden, cuda_device):
+    """With P kept at ~16 bits (exact_p), every golden, outlier cases included, meets the north-star bound as
+    stated: max-abs 2e-3 (fp16) / 1e-2 (bf16) against the reference's fp32 output, no P-rounding allowance."""
+    from mxflashattn_b200 import backend
+
+    case = VARLEN_GOLDEN[name]
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out = backend.flash_attn_varlen_func(q, k, v, cu_q, cu_k, int(np.diff(case.cu_q).max()),
+                                         int(np.diff(case.cu_k).max()), case.causal, case.softmax_scale,
+                                         exact_p=True)
+    assert_close_out(host(out), golden[f"{name}.out_f32"], case.dtype, name + " (exact P, strict)")
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_exact_p_outliers_within_north_star_bound_without_allowance(dt, d, cuda_device):
+    """The coverage matrix's value distribution (1% of K/V entries x50) over several key tiles, every row and head,
+    output and LSE, at the plain north-star bound with exact_p."""
+    from mxflashattn_b200 import backend
+
+    case = syn.varlen_case(70 + d, q_lens=[300, 77, 1000], q_heads=8, kv_heads=2, head_dim=d, dtype=dt,
+                           causal=True, outlier_frac=0.01)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+    out, lse = backend.flash_attn_varlen_func(q, k, v, cu_q, cu_k, 1000, 1000, True, case.softmax_scale,
+                                              return_lse=True, exact_p=True)
+    ref, ref_lse = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k,
+                                           softmax_scale=case.softmax_scale, causal=True, return_lse=True)
+    assert_close_out(host(out), ref, dt, f"outliers {dt} d{d} (exact P, strict)")
+    assert_close_lse(host(lse), np.asarray(ref_lse).T, f"outliers {dt} d{d} (exact P) LSE")  # oracle LSE is [H, T]
+
+
 @pytest.mark.parametrize("name", ["varlen_causal_bf16", "varlen_causal_d128_gq4"])
 def test_varlen_lse(name, golden, cuda_device):
     from mxflashattn_b200 import backend
