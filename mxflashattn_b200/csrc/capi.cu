@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include <cstdlib>
 
@@ -238,56 +239,78 @@ bool encode_kv_map_fp8(CUtensorMap* map, const void* k, const void* v, int HKV, 
   return true;
 }
 
-// Encoded K/V tensor maps of recently used caches, keyed by everything the
-// encoding reads (addresses, head dim, heads, slot rows, element type), so a
-// decode call reuses them instead of re-encoding (one driver call each).  A
-// small fixed table per device with round-robin replacement.
+// Encoded tensor maps of recently used operands, keyed by everything the
+// encoding reads (device, addresses, shape, element type), so a call reuses
+// them instead of re-encoding (one driver call per map).  Hash tables per
+// kind, bounded: when one reaches its limit it is cleared and refilled, so a
+// model with many layers' caches still hits on every call after the first.
+struct MapKey {
+  int device;
+  const void *a, *b, *c;
+  long long n0, n1, n2, n3;
+  bool operator==(const MapKey& o) const {
+    return device == o.device && a == o.a && b == o.b && c == o.c && n0 == o.n0 && n1 == o.n1 && n2 == o.n2 &&
+           n3 == o.n3;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<int>()(k.device);
+    auto mix = [&h](size_t v) { h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2); };
+    mix(std::hash<const void*>()(k.a));
+    mix(std::hash<const void*>()(k.b));
+    mix(std::hash<const void*>()(k.c));
+    mix(std::hash<long long>()(k.n0));
+    mix(std::hash<long long>()(k.n1));
+    mix(std::hash<long long>()(k.n2));
+    mix(std::hash<long long>()(k.n3));
+    return h;
+  }
+};
+template <typename V>
+struct MapCache {
+  std::mutex mu;
+  std::unordered_map<MapKey, V, MapKeyHash> table;
+  size_t limit;
+  explicit MapCache(size_t lim) : limit(lim) {}
+  bool get(const MapKey& k, V* out) {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = table.find(k);
+    if (it == table.end()) return false;
+    *out = it->second;
+    return true;
+  }
+  void put(const MapKey& k, const V& v) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (table.size() >= limit) table.clear();
+    table[k] = v;
+  }
+};
+
 struct KvMaps {
   CUtensorMap tk{}, tv{};
   int kind = 0, swap = 0;
   bool tma = false;
 };
-struct KvMapEntry {
-  int device = -1;
-  const void *k = nullptr, *v = nullptr;
-  int D = 0, HKV = 0;
-  long long slots = 0;
-  bool fp8 = false;
-  KvMaps maps;
-};
-constexpr int kKvMapCache = 64;
-std::mutex g_kv_map_mu;
-KvMapEntry g_kv_maps[kKvMapCache];
-int g_kv_map_next = 0;
+MapCache<KvMaps> g_kv_maps(8192);
 
 bool kv_map_cache_get(const void* k, const void* v, int D, int HKV, long long slots, bool fp8, KvMaps* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  std::lock_guard<std::mutex> lock(g_kv_map_mu);
-  for (const KvMapEntry& e : g_kv_maps) {
-    if (e.device == dev && e.k == k && e.v == v && e.D == D && e.HKV == HKV && e.slots == slots && e.fp8 == fp8) {
-      *out = e.maps;
-      return true;
-    }
-  }
-  return false;
+  return g_kv_maps.get(MapKey{dev, k, v, nullptr, D, HKV, slots, fp8 ? 1 : 0}, out);
 }
 
 void kv_map_cache_put(const void* k, const void* v, int D, int HKV, long long slots, bool fp8, const KvMaps& maps) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return;
-  std::lock_guard<std::mutex> lock(g_kv_map_mu);
-  KvMapEntry& e = g_kv_maps[g_kv_map_next];
-  g_kv_map_next = (g_kv_map_next + 1) % kKvMapCache;
-  e.device = dev;
-  e.k = k;
-  e.v = v;
-  e.D = D;
-  e.HKV = HKV;
-  e.slots = slots;
-  e.fp8 = fp8;
-  e.maps = maps;
+  g_kv_maps.put(MapKey{dev, k, v, nullptr, D, HKV, slots, fp8 ? 1 : 0}, maps);
 }
+
+// The three maps of a prefill call (q, k, v rows).
+struct PrefillMaps {
+  CUtensorMap q{}, k{}, v{};
+};
+MapCache<PrefillMaps> g_prefill_maps(4096);
 
 // Runs the decode kernel (split or direct) for a validated configuration;
 // kv_fp8: the caches hold e4m3 (D = 128 only).
@@ -888,10 +911,21 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // TMA maps cover exactly the token rows of q and k/v: boxes reaching past
   // the last row read zeros instead of memory beyond the tensors
-  CUtensorMap mq, mk, mv;
-  if (!encode_rows_map(&mq, q, D, HQ, total_q, kTcRows) || !encode_rows_map(&mk, k, D, HKV, total_k, kTcKeys) ||
-      !encode_rows_map(&mv, v, D, HKV, total_k, kTcKeys))
-    return fail(MXFA_ERR_UNSUPPORTED, "TMA descriptor encoding failed for the prefill operands");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key{dev, q, k, v, D, HQ, (static_cast<long long>(HKV) << 32) | static_cast<unsigned>(total_q),
+                   total_k};
+  PrefillMaps maps;
+  if (!g_prefill_maps.get(key, &maps)) {
+    if (!encode_rows_map(&maps.q, q, D, HQ, total_q, kTcRows) ||
+        !encode_rows_map(&maps.k, k, D, HKV, total_k, kTcKeys) ||
+        !encode_rows_map(&maps.v, v, D, HKV, total_k, kTcKeys))
+      return fail(MXFA_ERR_UNSUPPORTED, "TMA descriptor encoding failed for the prefill operands");
+    g_prefill_maps.put(key, maps);
+  }
+  const CUtensorMap& mq = maps.q;
+  const CUtensorMap& mk = maps.k;
+  const CUtensorMap& mv = maps.v;
   dim3 grid(HQ, B, (max_q + kTcRows - 1) / kTcRows);
   auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done, int threads) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;

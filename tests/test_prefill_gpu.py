@@ -281,3 +281,20 @@ def test_many_sequences_with_keys_longer_than_queries(cuda_device):
     ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, causal=True)
     abs_v = oracle.attention_varlen(case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, causal=True)
     assert_close_out(host(out), ref, "bf16", "many sequences, k longer than q", extra=p_rounding_bound("bf16", abs_v))
+
+
+def test_cached_tensor_maps_follow_the_shape_at_the_same_address(cuda_device):
+    """The library caches the prefill operands' TMA descriptors by address and shape: two calls on the same buffers
+    with different row counts must each see their own rows (a map cached for the shorter call would read zeros)."""
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    big = syn.varlen_case(81, q_lens=[500], q_heads=8, kv_heads=2, head_dim=128, dtype="bf16", causal=True)
+    q, k, v, _, _ = _dev(big, cuda_device)
+    for n in (300, 500, 300):
+        cu = torch.tensor([0, n], dtype=torch.int32, device=cuda_device)
+        out = backend.flash_attn_varlen_func(q[:n], k[:n], v[:n], cu, cu, n, n, True, big.softmax_scale)
+        ref = oracle.attention_varlen(big.q[:n], big.k[:n], big.v[:n], np.array([0, n], np.int32),
+                                      np.array([0, n], np.int32), softmax_scale=big.softmax_scale, causal=True)
+        assert_close_out(host(out), ref, "bf16", f"rows {n}")
