@@ -180,11 +180,12 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
  * sequence's pages.  Per call:
  *   mxfa_cp_decode_launch  split decode of the local range; the merging CTA of
  *                          each (sequence, KV head) writes its normalised
- *                          (O, LSE) record into EVERY rank's exchange buffer
- *                          (plain NVLink stores) and raises a flag there;
- *   mxfa_cp_merge_launch   on each rank: wait (bounded) for all ranks' flags,
- *                          LSE-merge the records in rank order, write out /
- *                          lse.
+ *                          (O, LSE) records into EVERY rank's exchange buffer
+ *                          (plain NVLink stores), each 32-bit value paired
+ *                          with the step's tag in one 64-bit word;
+ *   mxfa_cp_merge_launch   on each rank: wait (bounded) until all ranks'
+ *                          words carry the step's tag, LSE-merge the records
+ *                          in rank order, write out / lse.
  * This replaces the NCCL all-gather of the records.  Exchange buffers come
  * from mxfa_peer_alloc (zeroed cudaMalloc) and are mapped on the other ranks
  * with mxfa_peer_export / mxfa_peer_import (CUDA IPC; no multicast).  One
@@ -208,6 +209,18 @@ int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cach
                           int bf16, float scale, void* stream);
 int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int B, int HQ, int HKV, int D, int bf16,
                          void* stream);
+/* Both steps from one call: the decode kernel's merging CTA of each unit also
+ * waits (bounded) for every rank's records of that unit and merges its rows into
+ * out / lse, so a layer is one launch.  That CTA holds its SM while it waits,
+ * so this is done only when the grid's units (B x HKV) are fewer than the
+ * CTAs the GPU holds at once; otherwise the call launches the decode and
+ * mxfa_cp_merge_launch as above.  local_buf: this rank's exchange buffer
+ * (the entry `rank` of peer_bufs, as a host-side pointer). */
+int mxfa_cp_attention_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                             const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                             unsigned int* counters, const unsigned long long* peer_bufs, void* local_buf, int rank,
+                             int world, int B, int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits,
+                             int chunk_len, int bf16, float scale, void* stream);
 
 /* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
  * counterpart in the reference.  It exists for callers that cannot allocate

@@ -163,14 +163,18 @@ class FusedContextParallelDecode:
 
     Same result as ``context_parallel_decode`` without the NCCL all-gather:
     each rank's decode publishes its records straight into every rank's
-    exchange buffer over NVLink (plain stores to CUDA-IPC-mapped memory), and
-    a small merge kernel on each rank waits for all ranks' flags and merges.
+    exchange buffer over NVLink (plain stores to CUDA-IPC-mapped memory);
+    the same kernel then waits for all ranks' records of each unit and merges
+    it (``one_launch``, when the grid's units fit on the GPU at once), or a
+    small merge kernel on each rank does (``one_launch=False``, and the
+    library's own choice for larger grids).
     One instance serves a fixed geometry (batch, heads, head dim) for any
     number of calls and layers; every rank must make the same calls in the
     same order.  ``close()`` (collective) releases the mappings.
     """
 
-    def __init__(self, batch: int, q_heads: int, kv_heads: int, head_dim: int, *, group=None, device=None):
+    def __init__(self, batch: int, q_heads: int, kv_heads: int, head_dim: int, *, group=None, device=None,
+                 one_launch: bool = True):
         import ctypes
 
         import torch
@@ -180,6 +184,7 @@ class FusedContextParallelDecode:
 
         self._lib = lib = _lib.load()
         self.group = group
+        self.one_launch = one_launch
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.geometry = (batch, q_heads, kv_heads, head_dim)
@@ -240,15 +245,23 @@ class FusedContextParallelDecode:
             ws = torch.empty((max(ws_bytes, 16) // 4,), device=q.device, dtype=torch.float32)
             counters = backend.split_counters(q.device, stream, int(lib.mxfa_split_counter_bytes(B, 1, HQ, HKV)))
             bf16 = int(q.dtype == torch.bfloat16)
-            rc = lib.mxfa_cp_decode_launch(
-                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), seq.data_ptr(),
-                out.data_ptr(), None, ws.data_ptr(), ws_bytes, counters.data_ptr(), self.peer_table.data_ptr(),
-                self.rank, self.world, B, HQ, HKV, D, PS, btw, k_cache.shape[0], num_splits, chunk_len, bf16,
-                float(scale), stream)
-            _lib.check(rc, "mxfa_cp_decode_launch")
-            rc = lib.mxfa_cp_merge_launch(self._local, out.data_ptr(), _lib.ptr(lse), self.world, B, HQ, HKV, D,
-                                          bf16, stream)
-            _lib.check(rc, "mxfa_cp_merge_launch")
+            if self.one_launch:
+                rc = lib.mxfa_cp_attention_launch(
+                    q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), seq.data_ptr(),
+                    out.data_ptr(), _lib.ptr(lse), ws.data_ptr(), ws_bytes, counters.data_ptr(),
+                    self.peer_table.data_ptr(), self._local, self.rank, self.world, B, HQ, HKV, D, PS, btw,
+                    k_cache.shape[0], num_splits, chunk_len, bf16, float(scale), stream)
+                _lib.check(rc, "mxfa_cp_attention_launch")
+            else:
+                rc = lib.mxfa_cp_decode_launch(
+                    q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), seq.data_ptr(),
+                    out.data_ptr(), None, ws.data_ptr(), ws_bytes, counters.data_ptr(), self.peer_table.data_ptr(),
+                    self.rank, self.world, B, HQ, HKV, D, PS, btw, k_cache.shape[0], num_splits, chunk_len, bf16,
+                    float(scale), stream)
+                _lib.check(rc, "mxfa_cp_decode_launch")
+                rc = lib.mxfa_cp_merge_launch(self._local, out.data_ptr(), _lib.ptr(lse), self.world, B, HQ, HKV,
+                                              D, bf16, stream)
+                _lib.check(rc, "mxfa_cp_merge_launch")
         return (out, lse) if return_lse else out
 
     def close(self) -> None:

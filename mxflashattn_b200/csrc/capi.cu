@@ -171,6 +171,10 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int D, int HKV, long long
 
 // ------------------------------------------------------------------ decode
 
+// Whether the last decode launch on this thread merged a context-parallel
+// step in place (cp_merge kept) or left the merge to cp_merge_kernel.
+thread_local int g_cp_merged = 0;
+
 template <typename T, int HD, int NT, bool kTma, bool kFp8 = false>
 int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv,
                        cudaStream_t st) {
@@ -178,6 +182,21 @@ int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, 
   auto kern = paged_decode_kernel<T, HD, NT, kTma, kFp8>;
   const int smem = DecodeCfg<HD, NT, kFp8>::kSmemBytes;
   if (int rc = ensure_smem(kern, smem, done)) return rc;
+  DecodeParams pl = p;
+  if (pl.cp_merge) {
+    // A unit's merging CTA waits for the other ranks while holding its SM
+    // slot.  With fewer units than resident CTAs the rest of the grid always
+    // has room to run, so every rank publishes every unit and every wait
+    // ends; otherwise the merge goes to its own kernel.
+    static std::atomic<int> per_sm{-1};
+    int occ = per_sm.load(std::memory_order_relaxed);
+    if (occ < 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kDecThreads, smem) != cudaSuccess) occ = 0;
+      per_sm.store(occ, std::memory_order_relaxed);
+    }
+    if (static_cast<long long>(pl.B) * grid.x >= static_cast<long long>(occ) * sm_count()) pl.cp_merge = 0;
+  }
+  g_cp_merged = pl.cp_merge;
   // programmatic dependent launch (the kernel waits for its predecessor
   // before reading inputs, and releases its successor early)
   cudaLaunchConfig_t cfg{};
@@ -190,7 +209,7 @@ int launch_decode_inst(const DecodeParams& p, dim3 grid, const CUtensorMap& tk, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pl, tk, tv);
   if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "paged_decode_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_kernel");
 }
@@ -600,7 +619,7 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
 
 size_t mxfa_cp_buffer_bytes(int world, int B, int HQ, int HKV, int D) {
   if (world <= 0 || B <= 0 || HKV <= 0 || HQ <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return 0;
-  return cp_layout(world, B * HKV, B * HQ, D).bytes;
+  return cp_layout(world, B * HQ, D).bytes;
 }
 
 int mxfa_peer_alloc(size_t bytes, void** ptr) {
@@ -646,11 +665,11 @@ int mxfa_peer_close(void* ptr) {
   return e == cudaSuccess ? MXFA_OK : fail(MXFA_ERR_CUDA, "IPC close: %s", cudaGetErrorString(e));
 }
 
-int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+static int cp_decode_impl(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
                           const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
                           unsigned* counters, const unsigned long long* peer_bufs, int rank, int world, int B,
                           int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits, int chunk_len,
-                          int bf16, float scale, void* stream) {
+                          int bf16, float scale, void* stream, void* local_buf) {
   if (peer_bufs == nullptr || counters == nullptr) return fail(MXFA_ERR_INVALID, "peer buffers / counters missing");
   if (world < 1 || world > 32 || rank < 0 || rank >= world)
     return fail(MXFA_ERR_INVALID, "rank %d of world %d (1..32 ranks)", rank, world);
@@ -695,8 +714,33 @@ int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cach
   p.cp_bufs = peer_bufs;
   p.cp_rank = rank;
   p.cp_world = world;
+  p.cp_merge = local_buf != nullptr ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return run_decode(p, D, bf16 != 0, st);
+  g_cp_merged = 0;
+  if (int rc = run_decode(p, D, bf16 != 0, st)) return rc;
+  if (local_buf == nullptr || g_cp_merged) return MXFA_OK;
+  return mxfa_cp_merge_launch(local_buf, out, lse, world, B, HQ, HKV, D, bf16, stream);
+}
+
+int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                          const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                          unsigned* counters, const unsigned long long* peer_bufs, int rank, int world, int B,
+                          int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits, int chunk_len,
+                          int bf16, float scale, void* stream) {
+  return cp_decode_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, counters,
+                        peer_bufs, rank, world, B, HQ, HKV, D, PS, BTW, num_pages, num_splits, chunk_len, bf16, scale,
+                        stream, nullptr);
+}
+
+int mxfa_cp_attention_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                             const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                             unsigned* counters, const unsigned long long* peer_bufs, void* local_buf, int rank,
+                             int world, int B, int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits,
+                             int chunk_len, int bf16, float scale, void* stream) {
+  if (local_buf == nullptr) return fail(MXFA_ERR_INVALID, "local exchange buffer missing");
+  return cp_decode_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, counters,
+                        peer_bufs, rank, world, B, HQ, HKV, D, PS, BTW, num_pages, num_splits, chunk_len, bf16, scale,
+                        stream, local_buf);
 }
 
 int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int B, int HQ, int HKV, int D, int bf16,
@@ -721,14 +765,14 @@ int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int 
   cudaError_t e;
   if (bf16)
     e = D == 128 ? cudaLaunchKernelEx(&cfg, cp_merge_kernel<__nv_bfloat16, 128>, buf,
-                                      static_cast<__nv_bfloat16*>(out), lse, rows, HQ, HQ / HKV, world, B * HKV)
+                                      static_cast<__nv_bfloat16*>(out), lse, rows, world)
                  : cudaLaunchKernelEx(&cfg, cp_merge_kernel<__nv_bfloat16, 64>, buf,
-                                      static_cast<__nv_bfloat16*>(out), lse, rows, HQ, HQ / HKV, world, B * HKV);
+                                      static_cast<__nv_bfloat16*>(out), lse, rows, world);
   else
     e = D == 128 ? cudaLaunchKernelEx(&cfg, cp_merge_kernel<__half, 128>, buf, static_cast<__half*>(out), lse, rows,
-                                      HQ, HQ / HKV, world, B * HKV)
+                                      world)
                  : cudaLaunchKernelEx(&cfg, cp_merge_kernel<__half, 64>, buf, static_cast<__half*>(out), lse, rows,
-                                      HQ, HQ / HKV, world, B * HKV);
+                                      world);
   if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "cp_merge_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("cp_merge_kernel");
 }

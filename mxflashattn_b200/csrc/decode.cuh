@@ -59,11 +59,17 @@ struct DecodeParams {
   // into scale_log2 by the launcher; v_scale multiplies the output.
   float v_scale;
   // Context-parallel exchange (optional, with counters): instead of writing
-  // out / lse, the merging CTA of a unit publishes its (O, LSE) record into
-  // the exchange buffer of every rank (peer memory) and raises its flag
-  // there; cp_merge_kernel on each rank completes the merge.
+  // out / lse, the merging CTA of a unit publishes its (O, LSE) records,
+  // tagged with the step, into the exchange buffer of every rank (peer
+  // memory).  With cp_merge the same CTA then waits (bounded) until every
+  // rank's records of its unit carry the step's tag, merges the unit's rows
+  // into out / lse, and the last unit advances the epoch; the launcher sets
+  // it only when every unit's merging CTA can wait while the rest of the
+  // grid still finds room, and otherwise cp_merge_kernel on each rank
+  // completes the merge.
   const unsigned long long* cp_bufs;  // [cp_world] exchange-buffer bases; [cp_rank] is local
   int cp_rank, cp_world;
+  int cp_merge;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -135,32 +141,34 @@ __device__ __forceinline__ int tile_slot_row(const DecodeParams& p, int b, int t
 
 // Exchange buffer of a context-parallel group (one per rank, allocated zeroed;
 // peers map it through CUDA IPC).  Every step (call) advances a device-side
-// epoch e and uses half e % 2 of the flags and records, so a rank that is one
-// step ahead never overwrites what a slower rank still reads:
-//   [0, 256)   header: epoch (u32), blocks done (u32)
-//   flags      [2][world][units] u32: flag[e%2][src][unit] = e + 1 once rank
-//              src published that unit's records for step e
-//   records    [2][world][rows][D + 1] f32: normalised O then natural-log LSE
+// epoch e and uses half e % 2 of the records, so a rank that is one step
+// ahead never overwrites what a slower rank still reads:
+//   [0, 256)   header: epoch (u32), merges done (u32)
+//   records    [2][world][rows][D + 2] u64 words: (tag e + 1) << 32 | value
+//              bits; words 0..D-1 the normalised O, word D the natural-log
+//              LSE, word D+1 padding (rows stay 16-byte aligned)
+// Each word carries its own step tag and is stored and loaded as one 64-bit
+// access (single-copy atomic), so a reader that sees the tag sees the value:
+// no flag, and no fence between the records and a flag, is needed.
 struct CpLayout {
-  size_t flags, flag_half, records, record_half, bytes;
+  size_t records, record_half, bytes;
 };
-__host__ __device__ inline CpLayout cp_layout(int world, int units, int rows, int D) {
+__host__ __device__ inline CpLayout cp_layout(int world, int rows, int D) {
   CpLayout l;
-  l.flags = 256;
-  l.flag_half = static_cast<size_t>(world) * units * 4;
-  l.records = (l.flags + 2 * l.flag_half + 255) / 256 * 256;
-  l.record_half = static_cast<size_t>(world) * rows * (D + 1) * 4;
+  l.records = 256;
+  l.record_half = static_cast<size_t>(world) * rows * (D + 2) * 8;
   l.bytes = l.records + 2 * l.record_half;
   return l;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ uint64_t cp_word(float v, unsigned tag) {
+  return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void st_words2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // Rows of one split's partial output, loaded as this lane's HD/32 columns.
@@ -305,22 +313,24 @@ __device__ __forceinline__ void merge_split_row(const float* ows, const float* m
 
 // kFp8: e4m3 caches.  Tiles are dequantised in registers (cvt e4m3x2 ->
 // f16x2, exact) and both products run in f16; q is converted to f16 once.
-// merge_split_row for the exchange: the normalised f32 row and its LSE are
-// written to the record slot [cp_rank][r] of every rank's exchange buffer.
+// merge_split_row for the exchange: the normalised f32 row and its LSE,
+// tagged with step tag, are written to the record slot [rank][r] of every
+// rank's exchange buffer (16-byte stores of two tagged words).
 template <int HD, bool kChunked = true>
 __device__ __forceinline__ void merge_split_row_publish(const float* ows, const float* mdws, int r, int NP,
                                                         int lane, const unsigned long long* bufs, int world,
-                                                        int rank, int rows, size_t rec_off) {
+                                                        int rank, int rows, size_t rec_off, unsigned tag) {
   constexpr int kPer = HD / 32;
   float acc[kPer], M, L;
   merge_split_core<HD, kChunked>(ows, mdws, r, NP, lane, acc, M, L);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const float lse = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
   for (int dst = 0; dst < world; ++dst) {
-    float* rec = reinterpret_cast<float*>(bufs[dst] + rec_off) + (static_cast<size_t>(rank) * rows + r) * (HD + 1);
+    uint64_t* rec = reinterpret_cast<uint64_t*>(bufs[dst] + rec_off) + (static_cast<size_t>(rank) * rows + r) * (HD + 2);
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) rec[lane * kPer + j] = acc[j] * inv;
-    if (lane == 0) rec[HD] = lse;
+    for (int j = 0; j < kPer; j += 2)
+      st_words2(rec + lane * kPer + j, cp_word(acc[j] * inv, tag), cp_word(acc[j + 1] * inv, tag));
+    if (lane == 0) st_words2(rec + HD, cp_word(lse, tag), cp_word(0.f, tag));
   }
 }
 
@@ -335,8 +345,65 @@ __device__ __noinline__ void merge_split_row_call(const float* ows, const float*
 template <int HD>
 __device__ __noinline__ void merge_split_row_publish_call(const float* ows, const float* mdws, int r, int NP,
                                                           int lane, const unsigned long long* bufs, int world,
-                                                          int rank, int rows, size_t rec_off) {
-  merge_split_row_publish<HD>(ows, mdws, r, NP, lane, bufs, world, rank, rows, rec_off);
+                                                          int rank, int rows, size_t rec_off, unsigned tag) {
+  merge_split_row_publish<HD>(ows, mdws, r, NP, lane, bufs, world, rank, rows, rec_off, tag);
+}
+
+// ------------------------------------------------ context-parallel merge
+
+// One query row (one warp): LSE-merge the world records of row r in rank
+// order, once each lane has seen step tag `tag` on its words (bounded wait:
+// after kWaitLimitNs from t0 the lane stops waiting, raises the timeout flag
+// and merges what it has), and write the output row and its LSE.  A record
+// (O, lse) is the partial (o = O, m = lse * log2 e, d = 1).
+template <typename T, int HD>
+__device__ __forceinline__ void cp_merge_row(const uint64_t* recs, int rows, int r, int world, int lane, T* out,
+                                             float* lse, unsigned tag, unsigned long long t0) {
+  constexpr int kPer = HD / 32;
+  float M = -INFINITY, L = 0.f;
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  bool late = false;
+  for (int src = 0; src < world; ++src) {
+    const uint64_t* rec = recs + (static_cast<size_t>(src) * rows + r) * (HD + 2);
+    uint64_t w[kPer], wl, pad;
+    for (;;) {
+      bool seen = true;
+#pragma unroll
+      for (int j = 0; j < kPer; j += 2) {
+        ld_words2(rec + lane * kPer + j, w[j], w[j + 1]);
+        seen = seen && static_cast<unsigned>(w[j] >> 32) == tag && static_cast<unsigned>(w[j + 1] >> 32) == tag;
+      }
+      ld_words2(rec + HD, wl, pad);
+      if (seen && static_cast<unsigned>(wl >> 32) == tag) break;
+      if (late || global_timer_ns() - t0 > kWaitLimitNs) {
+        if (!late) raise_flag(MXFA_FLAG_WAIT_TIMEOUT);
+        late = true;
+        break;
+      }
+    }
+    const float mz = __uint_as_float(static_cast<uint32_t>(wl)) * kLog2e;
+    if (!(mz > -INFINITY)) continue;
+    const float mn = fmaxf(M, mz);
+    const float f1 = fast_exp2(M - mn);
+    const float f2 = fast_exp2(mz - mn);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) acc[j] = acc[j] * f1 + __uint_as_float(static_cast<uint32_t>(w[j])) * f2;
+    L = L * f1 + f2;
+    M = mn;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
+#pragma unroll
+  for (int j = 0; j < kPer; j += 2)
+    *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
+  if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+}
+template <typename T, int HD>
+__device__ __noinline__ void cp_merge_row_call(const uint64_t* recs, int rows, int r, int world, int lane, T* out,
+                                               float* lse, unsigned tag, unsigned long long t0) {
+  cp_merge_row<T, HD>(recs, rows, r, world, lane, out, lse, tag, t0);
 }
 
 // e4m3 tiles: token order of the score product.  ldmatrix .m16n16 .trans
@@ -952,9 +1019,11 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
     if (s_last) {
       __threadfence();
       const int rows_all = p.B * p.Sq * p.HQ;
-      const CpLayout lay = cp_layout(p.cp_world, p.B * gridDim.x, rows_all, HD);
+      const CpLayout lay = cp_layout(p.cp_world, rows_all, HD);
       const unsigned epoch =
           p.cp_bufs != nullptr ? *reinterpret_cast<const volatile unsigned*>(p.cp_bufs[p.cp_rank]) : 0u;
+      const unsigned tag = epoch + 1u;
+      const size_t rec_off = lay.records + (epoch & 1u) * lay.record_half;
       for (int col = warp; col < Mg::kCols; col += kDecConsumerWarps) {
         const int rr = row_base + col;
         if (rr >= rows_total) break;
@@ -965,24 +1034,40 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
           // the e4m3 kernel runs at its register cap: the loop form, inline
           if (p.cp_bufs != nullptr)
             merge_split_row_publish<HD, false>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank,
-                                               rows_all, lay.records + (epoch & 1u) * lay.record_half);
+                                               rows_all, rec_off, tag);
           else
             merge_split_row<T, HD, false>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), nullptr, p.lse);
         } else if (p.cp_bufs != nullptr) {
           merge_split_row_publish_call<HD>(p.ows, p.mdws, R, p.NP, lane, p.cp_bufs, p.cp_world, p.cp_rank, rows_all,
-                                           lay.records + (epoch & 1u) * lay.record_half);
+                                           rec_off, tag);
         } else {
           merge_split_row_call<T, HD>(p.ows, p.mdws, R, p.NP, lane, static_cast<T*>(p.out), p.lse);
         }
       }
-      if (p.cp_bufs != nullptr) {
-        // every writer's records reach every rank before its flag does
-        __threadfence_system();
-        named_barrier_sync(1, kDecConsumerWarps * 32);
-        if (tid < p.cp_world) {
-          const unsigned unit = static_cast<unsigned>(b) * gridDim.x + blockIdx.x;
-          unsigned* flags = reinterpret_cast<unsigned*>(p.cp_bufs[tid] + lay.flags + (epoch & 1u) * lay.flag_half);
-          st_release_sys(flags + static_cast<size_t>(p.cp_rank) * p.B * gridDim.x + unit, epoch + 1u);
+      if constexpr (!kFp8) {
+        if (p.cp_bufs != nullptr && p.cp_merge) {
+          // Merge this unit's rows as soon as every rank's words for them carry
+          // this step's tag (each warp reads back the rows it published, so the
+          // local record needs no ordering beyond program order).
+          unsigned char* local = reinterpret_cast<unsigned char*>(p.cp_bufs[p.cp_rank]);
+          const uint64_t* recs = reinterpret_cast<const uint64_t*>(local + rec_off);
+          const unsigned long long t0 = global_timer_ns();
+          for (int col = warp; col < Mg::kCols; col += kDecConsumerWarps) {
+            const int rr = row_base + col;
+            if (rr >= rows_total) break;
+            const int h = kvh * p.GQ + rr % p.GQ;
+            const int R = (b * p.Sq + rr / p.GQ) * p.HQ + h;
+            cp_merge_row_call<T, HD>(recs, rows_all, R, p.cp_world, lane, static_cast<T*>(p.out), p.lse, tag, t0);
+          }
+          named_barrier_sync(1, kDecConsumerWarps * 32);
+          if (tid == 0) {
+            __threadfence();
+            unsigned* hdr = reinterpret_cast<unsigned*>(local);
+            if (atomicAdd(hdr + 1, 1u) == static_cast<unsigned>(p.B * gridDim.x) - 1u) {  // every unit merged
+              hdr[1] = 0u;
+              *reinterpret_cast<volatile unsigned*>(hdr) = epoch + 1u;
+            }
+          }
         }
       }
       if (tid == 0) *counter = 0u;  // ready for the next launch on this stream
@@ -1066,63 +1151,25 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const float* __restr
   }
 }
 
-// ------------------------------------------------ context-parallel merge
+// ------------------------------------- context-parallel merge, second launch
 
-// One warp per query row on each rank: wait (bounded) until every rank's
-// flag for the row's unit shows this step, then LSE-merge the world records
-// of the row in rank order (the algebra of the packed merge above) and write
-// the output.  The last block to finish advances the epoch.
+// The merge as its own kernel, for grids whose units do not all fit on the
+// GPU at once (the decode kernel merges in place otherwise).  One warp per
+// query row on each rank merges the row's records once every rank's words
+// carry this step's tag (bounded wait).  The last block to finish advances
+// the epoch.
 template <typename T, int HD>
 __global__ void __launch_bounds__(128) cp_merge_kernel(unsigned char* buf, T* __restrict__ out,
-                                                       float* __restrict__ lse, int rows, int HQ, int GQ, int world,
-                                                       int units) {
-  constexpr int kPer = HD / 32;
+                                                       float* __restrict__ lse, int rows, int world) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   unsigned* hdr = reinterpret_cast<unsigned*>(buf);
   const unsigned epoch = *reinterpret_cast<volatile unsigned*>(hdr);
-  const CpLayout lay = cp_layout(world, units, rows, HD);
-  if (r < rows) {
-    // row r = b * HQ + h belongs to unit (b, h / GQ); units are numbered b * (HQ / GQ) + h / GQ
-    const int unit = (r / HQ) * (HQ / GQ) + (r % HQ) / GQ;
-    const unsigned* flags = reinterpret_cast<const unsigned*>(buf + lay.flags + (epoch & 1u) * lay.flag_half);
-    bool ready = lane >= world;
-    const unsigned long long t0 = global_timer_ns();
-    while (!__all_sync(0xffffffffu, ready)) {
-      if (!ready) ready = ld_acquire_sys(flags + static_cast<size_t>(lane) * units + unit) == epoch + 1u;
-      // lane 0's clock decides for the whole warp, so every lane leaves the
-      // loop together and the next __all_sync is always warp-complete
-      const bool late = __shfl_sync(0xffffffffu, global_timer_ns() - t0 > kWaitLimitNs, 0);
-      if (late) {
-        if (lane == 0) raise_flag(MXFA_FLAG_WAIT_TIMEOUT);
-        break;
-      }
-    }
-    __syncwarp();  // each lane acquired one rank's flag; the warp barrier shares what they saw
-    const float* recs = reinterpret_cast<const float*>(buf + lay.records + (epoch & 1u) * lay.record_half);
-    float M = -INFINITY, L = 0.f;
-    float acc[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
-    for (int src = 0; src < world; ++src) {
-      const float* rec = recs + (static_cast<size_t>(src) * rows + r) * (HD + 1);
-      const float mz = __ldcg(rec + HD) * kLog2e;  // (O, lse) == (o = O, m = lse*log2e, d = 1)
-      if (!(mz > -INFINITY)) continue;
-      const float mn = fmaxf(M, mz);
-      const float f1 = fast_exp2(M - mn);
-      const float f2 = fast_exp2(mz - mn);
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) acc[j] = acc[j] * f1 + __ldcg(rec + lane * kPer + j) * f2;
-      L = L * f1 + f2;
-      M = mn;
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* op = out + static_cast<size_t>(r) * HD + lane * kPer;
-#pragma unroll
-    for (int j = 0; j < kPer; j += 2) *reinterpret_cast<uint32_t*>(op + j) = Elem<T>::pack(acc[j] * inv, acc[j + 1] * inv);
-    if (lse != nullptr && lane == 0) lse[r] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
-  }
+  const CpLayout lay = cp_layout(world, rows, HD);
+  if (r < rows)
+    cp_merge_row<T, HD>(reinterpret_cast<const uint64_t*>(buf + lay.records + (epoch & 1u) * lay.record_half), rows,
+                        r, world, lane, out, lse, epoch + 1u, global_timer_ns());
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();

@@ -213,6 +213,36 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+#define MXFA_RW32(x)                                                                                            \
+  "+r"(x[0]), "+r"(x[1]), "+r"(x[2]), "+r"(x[3]), "+r"(x[4]), "+r"(x[5]), "+r"(x[6]), "+r"(x[7]), "+r"(x[8]),   \
+      "+r"(x[9]), "+r"(x[10]), "+r"(x[11]), "+r"(x[12]), "+r"(x[13]), "+r"(x[14]), "+r"(x[15]), "+r"(x[16]),    \
+      "+r"(x[17]), "+r"(x[18]), "+r"(x[19]), "+r"(x[20]), "+r"(x[21]), "+r"(x[22]), "+r"(x[23]), "+r"(x[24]),   \
+      "+r"(x[25]), "+r"(x[26]), "+r"(x[27]), "+r"(x[28]), "+r"(x[29]), "+r"(x[30]), "+r"(x[31])
+
+// Split load: the registers are written asynchronously and are valid only
+// after tmem_wait_ld on the same array, whose read-write operands keep every
+// use of them behind the wait.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : MXFA_R32(r)
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : MXFA_RW32(r) : : "memory");
+}
+// Store without waiting; tmem_wait_st before the values are handed over.
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      MXFA_W16(r)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // 16 / 8 consecutive 32-bit columns (the masked softmax path works in
 // 16-column chunks so its code stays small).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -230,6 +260,57 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
       "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
+}
+
+// Two fp32 lanes in one 64-bit register, for the packed fp32 instructions
+// (fma/add .f32x2): one instruction per pair of scores in the softmax.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// P = 2^(s*scale - m) for 32 columns of one row: packed into 16 words of
+// the element type, summed into two pair accumulators.
+template <typename T>
+__device__ __forceinline__ void exp2_chunk32(const uint32_t (&x)[32], uint64_t sc2, uint64_t nm2, uint64_t& acc0,
+                                             uint64_t& acc1, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const uint64_t x01 = f2_fma(f2_pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sc2, nm2);
+    const uint64_t x23 = f2_fma(f2_pack(__uint_as_float(x[i + 2]), __uint_as_float(x[i + 3])), sc2, nm2);
+    float a, b, c, d;
+    f2_unpack(x01, a, b);
+    f2_unpack(x23, c, d);
+    a = fast_exp2(a);
+    b = fast_exp2(b);
+    c = fast_exp2(c);
+    d = fast_exp2(d);
+    acc0 = f2_add(acc0, f2_pack(a, b));
+    acc1 = f2_add(acc1, f2_pack(c, d));
+    pk[i >> 1] = Elem<T>::pack(a, b);
+    pk[(i >> 1) + 1] = Elem<T>::pack(c, d);
+  }
+}
+// Row extreme (max for a positive scale, min for a negative one) of 32 columns, four chains.
+__device__ __forceinline__ void ext_chunk32(const uint32_t (&x)[32], bool pos, float (&e)[4]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float v = __uint_as_float(x[i]);
+    e[i & 3] = pos ? fmaxf(e[i & 3], v) : fminf(e[i & 3], v);
+  }
 }
 
 // Shared-memory matrix descriptor: 128-byte swizzle, descriptor version 1.
@@ -336,6 +417,14 @@ struct TcBars {
 // rescaling softmax group).  No barrier is waited on more than one phase
 // ahead of its state; the epilogue, which a group can reach while the last
 // tile's buffer is still two phases behind, waits on a one-shot barrier.
+//
+// On a tile every row sees in full, the softmax reads S in 32-column loads
+// whose wait is split from the load, so each load is in flight while the
+// previous chunk is worked on; the last chunk of the maximum pass stays in
+// registers and the exp2 pass's first load is issued before the maximum
+// exchange.  The exp2 pass scales and sums two scores per instruction
+// (fma/add .f32x2).  At the power cap fewer instructions are also a higher
+// clock.
 // kExactP: P is split into its rounded value and the rounded remainder,
 // P_hi + P_lo (~16 significant bits), stored side by side in S's columns
 // (per 16-key chunk: 8 columns of P_hi, then 8 of P_lo) and both multiplied
@@ -560,22 +649,26 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
       const bool pos = sc >= 0.f;
       const float ext0 = pos ? -INFINITY : INFINITY;
       float ext = ext0;
+      uint32_t ra[32], rb[32];
       if (all_full) {
-        // four independent chains, so the compare latency overlaps
-        float e0 = ext0, e1 = ext0, e2 = ext0, e3 = ext0;
-#pragma unroll 1
-        for (int c = 0; c < kTcKeys; c += 64) {
-          uint32_t raw[64];
-          tmem_ld64(sbuf + c, raw);
-#pragma unroll
-          for (int i = 0; i < 64; i += 4) {
-            e0 = pos ? fmaxf(e0, __uint_as_float(raw[i])) : fminf(e0, __uint_as_float(raw[i]));
-            e1 = pos ? fmaxf(e1, __uint_as_float(raw[i + 1])) : fminf(e1, __uint_as_float(raw[i + 1]));
-            e2 = pos ? fmaxf(e2, __uint_as_float(raw[i + 2])) : fminf(e2, __uint_as_float(raw[i + 2]));
-            e3 = pos ? fmaxf(e3, __uint_as_float(raw[i + 3])) : fminf(e3, __uint_as_float(raw[i + 3]));
-          }
-        }
-        ext = pos ? fmaxf(fmaxf(e0, e1), fmaxf(e2, e3)) : fminf(fminf(e0, e1), fminf(e2, e3));
+        // 32-column loads, each in flight while the previous chunk is
+        // compared (four chains).  The last chunk stays in registers for
+        // pass 2, whose first load goes out before the maximum exchange.
+        float e[4] = {ext0, ext0, ext0, ext0};
+        tmem_ld32_async(sbuf, ra);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 32, rb);
+        ext_chunk32(ra, pos, e);
+        tmem_wait_ld(rb);
+        tmem_ld32_async(sbuf + 64, ra);
+        ext_chunk32(rb, pos, e);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 96, rb);
+        ext_chunk32(ra, pos, e);
+        tmem_wait_ld(rb);
+        if constexpr (!kExactP) tmem_ld32_async(sbuf, ra);
+        ext_chunk32(rb, pos, e);
+        ext = pos ? fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])) : fminf(fminf(e[0], e[1]), fminf(e[2], e[3]));
       } else {
         // diagonal tile: a rolled loop over 16-column chunks keeps this
         // rarely taken path out of the way of the unrolled one
@@ -633,8 +726,8 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
         }
       }
 
-      // pass 2: P = 2^(s*scale - m_j) over each 64-key half, packed in pairs
-      // into the 32 columns of S that the halves before it already consumed
+      // pass 2: P = 2^(s*scale - m_j), packed in pairs into columns of S
+      // that were already read
       float rs = 0.f;
       const float neg_m = -m_j;
       if (kExactP && all_full) {
@@ -687,28 +780,31 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
           tmem_st16(sbuf + c, packed);
         }
       } else if (all_full) {  // every row sees every key of the tile, so m_j is finite
-        float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < kTcKeys; c += 64) {
-          uint32_t raw[64];
-          tmem_ld64(sbuf + c, raw);
-          uint32_t packed[32];
-#pragma unroll
-          for (int i = 0; i < 64; i += 4) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m));
-            const float p2 = fast_exp2(fmaf(__uint_as_float(raw[i + 2]), sc, neg_m));
-            const float p3 = fast_exp2(fmaf(__uint_as_float(raw[i + 3]), sc, neg_m));
-            r0 += p0;
-            r1 += p1;
-            r2 += p2;
-            r3 += p3;
-            packed[i >> 1] = Elem<T>::pack(p0, p1);
-            packed[(i >> 1) + 1] = Elem<T>::pack(p2, p3);
-          }
-          tmem_st32(sbuf + (c >> 1), packed);
-        }
-        rs = (r0 + r1) + (r2 + r3);
+        // rb holds columns 96-127 from pass 1 and ra's load of columns 0-31
+        // is in flight; each later load overlaps the previous chunk's exp2.
+        // P of columns [32k, 32k+32) goes to columns [16k, 16k+16), which
+        // lie in columns already read; the stores are waited on once.
+        const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc0 = 0, acc1 = 0;  // four sum chains: columns i % 4
+        uint32_t pk3[16], pka[16], pkb[16];
+        exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pk3);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 32, rb);
+        exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
+        tmem_st16_async(sbuf, pka);
+        tmem_wait_ld(rb);
+        tmem_ld32_async(sbuf + 64, ra);
+        exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pkb);
+        tmem_st16_async(sbuf + 16, pkb);
+        tmem_st16_async(sbuf + 48, pk3);  // columns 48-63 were read with chunk 1
+        tmem_wait_ld(ra);
+        tmem_wait_st();  // pka is written again below
+        exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
+        tmem_st16_async(sbuf + 32, pka);
+        tmem_wait_st();
+        float a, bb;
+        f2_unpack(f2_add(acc0, acc1), a, bb);
+        rs = a + bb;
       } else {
         const bool live = m_j != -INFINITY;
 #pragma unroll 1
@@ -734,6 +830,7 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[buf]);
     }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");  // a load left in flight by an aborted tile
 
     // ---------------------------------------------------------- merge + store
     // Every product is complete once the last P.V is; the Q tile's shared

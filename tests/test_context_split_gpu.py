@@ -78,8 +78,11 @@ def _nccl_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-def _fused_worker(rank, world, port, result):
-    """Fused exchange vs the NCCL path and the oracle, over three calls (both buffer halves)."""
+def _fused_worker(rank, world, port, result, modes=(True,)):
+    """Fused exchange vs the NCCL path and the oracle, over three calls (both buffer halves).
+
+    ``modes`` cycles the exchange form per call: True merges inside the decode
+    kernel (one launch), False in the separate merge kernel."""
     import torch
     import torch.distributed as dist
 
@@ -100,7 +103,8 @@ def _fused_worker(rank, world, port, result):
         bt = torch.from_numpy(table).to(dev)
         fused = cs.FusedContextParallelDecode(4, 32, 8, 128, device=dev)
         worst = -1.0
-        for step in range(3):
+        for step in range(4):
+            fused.one_launch = modes[step % len(modes)]
             q_np = case.q if step == 0 else syn.round_dtype(np.random.default_rng(50 + step).standard_normal(
                 case.q.shape).astype(np.float32), "bf16")
             q = torch.from_numpy(q_np).to(dev, tdt)
@@ -122,7 +126,8 @@ def _fused_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-def test_two_gpu_fused_peer_exchange(cuda_device):
+@pytest.mark.parametrize("modes", [(True,), (False,), (True, False)], ids=["one_launch", "two_launches", "mixed"])
+def test_two_gpu_fused_peer_exchange(cuda_device, modes):
     import torch
     import torch.multiprocessing as mp
 
@@ -133,13 +138,17 @@ def test_two_gpu_fused_peer_exchange(cuda_device):
         port = s.getsockname()[1]
     manager = mp.Manager()
     result = manager.dict()
-    mp.spawn(_fused_worker, args=(2, port, result), nprocs=2, join=True)
+    mp.spawn(_fused_worker, args=(2, port, result, modes), nprocs=2, join=True)
     assert all(result[r] <= 0.0 for r in range(2)), dict(result)
     assert all(result[f"flags{r}"] == 0 for r in range(2)), dict(result)
 
 
-def test_single_rank_fused_exchange_matches_local_decode(cuda_device):
-    """world = 1: the exchange degenerates to the local record (no peer, no waiting on another device)."""
+@pytest.mark.parametrize("modes", [(True,), (False,), (True, False)], ids=["one_launch", "two_launches", "mixed"])
+def test_single_rank_fused_exchange_matches_local_decode(cuda_device, modes):
+    """world = 1: the exchange degenerates to the local record (no peer, no waiting on another device).
+
+    Both exchange forms, and the two alternating on one buffer (their epoch
+    and counters must hand over cleanly), against the oracle, LSE included."""
     import datetime as _dt
     import os
 
@@ -161,11 +170,56 @@ def test_single_rank_fused_exchange_matches_local_decode(cuda_device):
         bt = torch.from_numpy(case.block_table).to(cuda_device)
         fused = cs.FusedContextParallelDecode(4, 32, 8, 128, device=cuda_device)
         try:
-            ref = oracle_paged(case)[0]
-            for _ in range(3):
-                out = fused(q, kc, vc, sl, bt, case.softmax_scale)
+            from mxflashattn_b200 import _lib
+
+            _lib.read_error_flags()  # clear what earlier tests left
+            ref, ref_lse = oracle_paged(case)[:2]
+            for step in range(5):
+                fused.one_launch = modes[step % len(modes)]
+                out, lse = fused(q, kc, vc, sl, bt, case.softmax_scale, return_lse=True)
                 torch.cuda.synchronize()
-                assert_close_out(host(out), ref, "bf16", "single-rank fused exchange")
+                assert_close_out(host(out), ref, "bf16", f"single-rank fused exchange, call {step}")
+                assert_close_lse(host(lse).reshape(ref_lse.shape), ref_lse, f"single-rank LSE, call {step}")
+            assert _lib.read_error_flags() == 0
+        finally:
+            fused.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_single_rank_exchange_with_more_units_than_resident_ctas(cuda_device):
+    """1024 units (128 sequences x 8 KV heads) exceed what one GPU holds at once, so the one-call
+    entry leaves the merge to its own kernel; the result still matches the oracle."""
+    import datetime as _dt
+
+    import torch
+    import torch.distributed as dist
+
+    from mxflashattn_b200 import _lib
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=_dt.timedelta(seconds=60))
+    try:
+        lengths = np.random.default_rng(7).integers(1, 300, size=128).tolist()
+        case = syn.paged_case(321, batch=128, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", page_size=16,
+                              lengths=lengths)
+        tdt = syn.torch_dtype(case.dtype)
+        args = [torch.from_numpy(a).to(cuda_device, tdt) for a in (case.q, case.k_cache, case.v_cache)]
+        sl = torch.from_numpy(case.cache_seqlens.copy()).to(cuda_device)
+        bt = torch.from_numpy(case.block_table).to(cuda_device)
+        fused = cs.FusedContextParallelDecode(128, 32, 8, 128, device=cuda_device)
+        try:
+            _lib.read_error_flags()
+            ref, ref_lse = oracle_paged(case)[:2]
+            for step in range(3):
+                out, lse = fused(*args, sl, bt, case.softmax_scale, return_lse=True)
+                torch.cuda.synchronize()
+                assert_close_out(host(out), ref, "bf16", f"128-sequence exchange, call {step}")
+                assert_close_lse(host(lse).reshape(ref_lse.shape), ref_lse, f"128-sequence LSE, call {step}")
+            assert _lib.read_error_flags() == 0
         finally:
             fused.close()
     finally:
@@ -191,8 +245,8 @@ def test_exchange_wait_times_out_and_reports(cuda_device):
     """A merge whose peer never publishes gives up after its bounded wait and raises the timeout flag.
 
     The exchange buffer is sized for two ranks but only this process exists, so
-    rank 1's flags are never set: every warp waits ~1 s, then the kernel
-    finishes, the context stays usable and the host reads the flag.
+    no record ever carries the step's tag: every warp waits ~1 s, then the
+    kernel finishes, the context stays usable and the host reads the flag.
     """
     import ctypes
     import time
