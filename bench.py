@@ -887,6 +887,7 @@ def extra_longctx(args, device, ranks):
                                                            locs[i][1], scale)
 
             g_f = capture(step_fused, device)
+            launches_fused = fused.launches_per_call  # 1: exchange and merge inside the decode kernel
             ms_f = time_graph(g_f, args.steps, args.warmup, device, ranks)
             g_n = capture(step_nccl, device)
             ms_n = time_graph(g_n, args.steps, args.warmup, device, ranks)
@@ -920,8 +921,10 @@ def extra_longctx(args, device, ranks):
                 "tolerance": {"out": 1e-2, "lse": 1e-3, "against": "one-GPU decode over the whole context"},
                 "parity_ok": bool(max(err_f, err_n) <= 1e-2 and max(lerr_f, lerr_n) <= 1e-3 and flags == 0),
                 "device_flags": int(flags),
-                "form": "fused NVLink peer-store exchange vs NCCL all-gather + merge, CUDA graph replay",
-                "gpu_launches_fused": args.steps * args.layers * 2,
+                "form": ("decode with the (O, LSE) exchange over NVLink peer stores and the merge in one kernel"
+                         if launches_fused == 1 else "decode with the exchange over NVLink peer stores + merge kernel")
+                        + " vs NCCL all-gather + merge kernel, CUDA graph replay",
+                "gpu_launches_fused": args.steps * args.layers * launches_fused,
             })
         res[f"b{B}"] = entry
         del full

@@ -221,6 +221,9 @@ int mxfa_cp_attention_launch(const void* q, const void* k_cache, const void* v_c
                              unsigned int* counters, const unsigned long long* peer_bufs, void* local_buf, int rank,
                              int world, int B, int HQ, int HKV, int D, int PS, int BTW, int num_pages, int num_splits,
                              int chunk_len, int bf16, float scale, void* stream);
+/* 1 when the calling thread's last mxfa_cp_attention_launch merged inside the
+ * decode kernel (one launch), 0 when it also launched the merge kernel. */
+int mxfa_cp_last_merged_in_place(void);
 
 /* Allocation-free variant of mxfa_kvcache_attention_launch.  It has no
  * counterpart in the reference.  It exists for callers that cannot allocate

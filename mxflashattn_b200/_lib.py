@@ -62,6 +62,7 @@ SIGNATURES = {
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _f, _vp]),
     "mxfa_cp_merge_launch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "mxfa_cp_last_merged_in_place": (_i, []),
     "mxfa_cp_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _i, _f, _vp]),

@@ -185,6 +185,7 @@ class FusedContextParallelDecode:
         self._lib = lib = _lib.load()
         self.group = group
         self.one_launch = one_launch
+        self.launches_per_call = 0  # kernels the last call launched (1: merged inside the decode kernel)
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.geometry = (batch, q_heads, kv_heads, head_dim)
@@ -252,6 +253,7 @@ class FusedContextParallelDecode:
                     self.peer_table.data_ptr(), self._local, self.rank, self.world, B, HQ, HKV, D, PS, btw,
                     k_cache.shape[0], num_splits, chunk_len, bf16, float(scale), stream)
                 _lib.check(rc, "mxfa_cp_attention_launch")
+                self.launches_per_call = 1 if lib.mxfa_cp_last_merged_in_place() else 2
             else:
                 rc = lib.mxfa_cp_decode_launch(
                     q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), seq.data_ptr(),
@@ -262,6 +264,7 @@ class FusedContextParallelDecode:
                 rc = lib.mxfa_cp_merge_launch(self._local, out.data_ptr(), _lib.ptr(lse), self.world, B, HQ, HKV,
                                               D, bf16, stream)
                 _lib.check(rc, "mxfa_cp_merge_launch")
+                self.launches_per_call = 2
         return (out, lse) if return_lse else out
 
     def close(self) -> None:

@@ -732,6 +732,8 @@ int mxfa_cp_decode_launch(const void* q, const void* k_cache, const void* v_cach
                         stream, nullptr);
 }
 
+int mxfa_cp_last_merged_in_place(void) { return g_cp_merged; }
+
 int mxfa_cp_attention_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
                              const int32_t* seqlens, void* out, float* lse, void* workspace, size_t workspace_bytes,
                              unsigned* counters, const unsigned long long* peer_bufs, void* local_buf, int rank,

@@ -180,6 +180,8 @@ def test_single_rank_fused_exchange_matches_local_decode(cuda_device, modes):
                 torch.cuda.synchronize()
                 assert_close_out(host(out), ref, "bf16", f"single-rank fused exchange, call {step}")
                 assert_close_lse(host(lse).reshape(ref_lse.shape), ref_lse, f"single-rank LSE, call {step}")
+                # 32 units fit on the GPU at once: the one-call form merges inside the decode kernel
+                assert fused.launches_per_call == (1 if fused.one_launch else 2)
             assert _lib.read_error_flags() == 0
         finally:
             fused.close()
@@ -219,6 +221,7 @@ def test_single_rank_exchange_with_more_units_than_resident_ctas(cuda_device):
                 torch.cuda.synchronize()
                 assert_close_out(host(out), ref, "bf16", f"128-sequence exchange, call {step}")
                 assert_close_lse(host(lse).reshape(ref_lse.shape), ref_lse, f"128-sequence LSE, call {step}")
+                assert fused.launches_per_call == 2  # the merge kernel ran
             assert _lib.read_error_flags() == 0
         finally:
             fused.close()
