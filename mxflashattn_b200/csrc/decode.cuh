@@ -870,7 +870,10 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
     // rounded high part and the rounded remainder (p = hi + lo to ~16
     // significant bits) and both are multiplied with V, so the product keeps
     // fp32-level accuracy even when V carries large outliers; the extra
-    // tensor-core work is free on this memory-bound path.
+    // tensor-core work is free on this memory-bound path.  The e4m3 path
+    // (instruction bound) multiplies the rounded P only: its f16 rounding
+    // (2^-11 relative) lies far below the e4m3 quantisation of the cache
+    // (2^-4 relative).
     uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -878,9 +881,11 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
       for (int hh = 0; hh < 2; ++hh) {
         const float a = s[nt][2 * hh], c = s[nt][2 * hh + 1];
         const uint32_t hi = Elem<MT>::pack(a, c);
-        const float2 hf = Elem<MT>::unpack(hi);
         pb[nt][hh] = movmatrix_trans(hi);
-        pl[nt][hh] = movmatrix_trans(Elem<MT>::pack(a - hf.x, c - hf.y));
+        if constexpr (!kFp8) {
+          const float2 hf = Elem<MT>::unpack(hi);
+          pl[nt][hh] = movmatrix_trans(Elem<MT>::pack(a - hf.x, c - hf.y));
+        }
       }
     if constexpr (kFp8) {
       // fp8 V through the transposing 8-bit ldmatrix: for head-dim step mi,
@@ -899,10 +904,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
           e4m3x4_to_f16x2x2(yy[h][0], a0, a2);  // d = 16*(mi+h) + g: token slots 2*t4.. and 2*t4+8..
           e4m3x4_to_f16x2x2(yy[h][1], a1, a3);  // d = 16*(mi+h) + g + 8
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            Elem<MT>::mma(o[mi + h][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-            Elem<MT>::mma(o[mi + h][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
-          }
+          for (int nt = 0; nt < NT; ++nt) Elem<MT>::mma(o[mi + h][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
       }
     } else {
