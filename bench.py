@@ -436,7 +436,11 @@ def build_layers(lengths, seed_base, layers, device, fp8=False):
 
 
 def decode_graph(layers, device):
-    """(graph, step, outs, plan) for one decode step over ``layers``."""
+    """(graph, step, plan) for one decode step over ``layers``.
+
+    The step first computes the batch's longest-first order once
+    (``kvcache_length_order``, one small kernel; None for a batch of one) and
+    every layer's launch takes it, as a model's decode step would."""
     import torch
 
     from mxflashattn_b200 import backend
@@ -449,11 +453,13 @@ def decode_graph(layers, device):
 
     def step(ev=None):
         stream = torch.cuda.current_stream(device)
+        order = backend.kvcache_length_order(layers[0]["cache_seqlens"])  # every layer has the same lengths
         for i, t in enumerate(layers):
             if ev is not None:
                 ev[2 * i].record(stream)
             backend.kvcache_attention(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
-                                      scale, False, num_splits=num_splits, chunk_len=chunk_len, out=outs[i])
+                                      scale, False, num_splits=num_splits, chunk_len=chunk_len, out=outs[i],
+                                      length_order=order)
             if ev is not None:
                 ev[2 * i + 1].record(stream)
 
@@ -470,7 +476,7 @@ def run_ours(args):
     torch.cuda.set_device(device)
     ranks = Ranks(world, rank, device)
 
-    from mxflashattn_b200 import flash_attn_with_kvcache, synthetic as syn
+    from mxflashattn_b200 import flash_attn_with_kvcache, kvcache_length_order, synthetic as syn
 
     lengths = syn.qwen3_4b_lengths(args.seed + rank, args.batch)
     fp8 = args.kv_dtype == "fp8"
@@ -482,6 +488,7 @@ def run_ours(args):
 
     graph, step, (num_splits, chunk_len) = decode_graph(layers, device)
     launches_per_layer = 1  # split plans merge in the same launch (counted single launch)
+    launches_per_step = 1 if 1 < args.batch <= 512 else 0  # the length order, once per step
     clocks = ClockSampler(device.index).start()
     elapsed_ms = time_graph(graph, args.steps, args.warmup, device, ranks, clocks)
     clocks.stop()
@@ -500,7 +507,8 @@ def run_ours(args):
     # --------------------------------------------------------------- e2e
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, layers, lengths, bytes_step, device, ranks, flash_attn_with_kvcache, scale)
+        e2e = run_e2e(args, layers, lengths, bytes_step, device, ranks, flash_attn_with_kvcache, scale,
+                      order_fn=kvcache_length_order)
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -532,7 +540,7 @@ def run_ours(args):
                      "avg_launch_ms": per_launch_ms},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
-        "gpu_launches": args.steps * args.layers * launches_per_layer,
+        "gpu_launches": args.steps * (args.layers * launches_per_layer + launches_per_step),
         "timing": "CUDA graph replay of the 36-layer step; e2e is eager through the public API",
     }
     del layers
@@ -551,7 +559,7 @@ def run_ours(args):
     ranks.close()
 
 
-def run_e2e(args, layers, lengths, bytes_step, device, ranks, api, scale):
+def run_e2e(args, layers, lengths, bytes_step, device, ranks, api, scale, order_fn=None):
     """The headline metric through the public API with host buffers, copies inside the timed region.
 
     Every step uploads that step's inputs (the 36 layers' q and the lengths)
@@ -587,9 +595,10 @@ def run_e2e(args, layers, lengths, bytes_step, device, ranks, api, scale):
             ev_up[p].record(h2d)
         stream.wait_event(ev_up[p])
         stream.wait_event(ev_down[p])  # ... and its outputs have left this buffer
+        kw = {} if order_fn is None else {"length_order": order_fn(sl_dev[p])}  # once per step
         for i, t in enumerate(layers):
             api(q_dev[p][i], t["k_cache"], t["v_cache"], cache_seqlens=sl_dev[p], block_table=t["block_table"],
-                softmax_scale=scale, out=out_dev[p][i])
+                softmax_scale=scale, out=out_dev[p][i], **kw)
         ev_used[p].record(stream)
         with torch.cuda.stream(d2h):
             d2h.wait_event(ev_used[p])
@@ -640,7 +649,8 @@ def run_e2e(args, layers, lengths, bytes_step, device, ranks, api, scale):
             "host_us_per_call": host_ms * 1e3 / (args.steps * len(layers)),
             "h2d_gbs_alone": q_bytes / (h2d_ms * 1e-3) / 1e9 if h2d_ms > 0 else None,
             "d2h_gbs_alone": o_bytes / (d2h_ms * 1e-3) / 1e9 if d2h_ms > 0 else None,
-            "method": "public flash_attn_with_kvcache per layer (out= a slot of the step's output buffer), eager; "
+            "method": "public flash_attn_with_kvcache per layer (out= a slot of the step's output buffer, "
+                      "length_order= from kvcache_length_order once per step), eager; "
                       "per step one upload of every layer's q and the lengths and one read-back of every layer's "
                       "output, on copy streams overlapping the neighbouring steps' kernels; *_gbs_alone = one "
                       "step's copies timed alone"}
@@ -669,7 +679,7 @@ def extra_fp8(args, lengths, device, ranks):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{kind} hbm_gbs",
                          "bytes_per_launch": bytes_layer, "bytes_rule": "1 B per cached e4m3 element"},
-            "num_splits": num_splits, "gpu_launches": args.steps * args.layers}
+            "num_splits": num_splits, "gpu_launches": args.steps * (args.layers + (1 < len(lengths) <= 512))}
 
 
 def extra_strong(args, device, ranks):

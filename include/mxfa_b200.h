@@ -40,6 +40,7 @@ extern "C" {
 #define MXFA_FLAG_TABLE_TOO_NARROW 0x2u   /* sequence longer than block_table width * page size */
 #define MXFA_FLAG_WAIT_TIMEOUT 0x4u       /* a bounded pipeline wait gave up */
 #define MXFA_FLAG_DENSE_OVERFLOW 0x8u     /* dense-cache append past the cache capacity */
+#define MXFA_FLAG_BAD_ORDER 0x10u         /* a length order entry outside [0, B) (that row ran its own index) */
 
 /* Library identity.  No reference counterpart (the reference's pybind
  * modules expose no version); used by the ctypes loader. */
@@ -153,6 +154,30 @@ int mxfa_kvcache_attention_fp8_launch(const void* q, const void* k_cache, const 
                                       int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
                                       int causal, int bf16, float scale, float k_scale, float v_scale,
                                       void* stream);
+
+/* Plan once per step, run per layer.  The decode kernel runs a batch's
+ * sequences longest first (1 < B <= 512): without an order every CTA ranks
+ * all B lengths before its first block-table read, on every layer.
+ * mxfa_kvcache_length_order_launch writes that order once (order[rank] =
+ * sequence, int32 [B], longest first, ties by index) from seqlens on the
+ * device; mxfa_kvcache_attention_ordered_launch then takes it in place of the
+ * ranking.  The order only schedules: lengths are always read from seqlens,
+ * so an order computed for other lengths of the same batch costs speed, not
+ * correctness; an entry outside [0, B) raises MXFA_FLAG_BAD_ORDER and that
+ * grid row runs its own index.  The ordered launch is
+ * mxfa_kvcache_attention_counted_launch (counters may be NULL: separate
+ * combine when the plan splits) or, with kv_fp8 = 1,
+ * mxfa_kvcache_attention_fp8_launch, plus length_order (NULL: the kernel
+ * ranks).  No reference counterpart (the reference launches the sequences in
+ * index order, m1_kernel.cpp:970-1021). */
+int mxfa_kvcache_length_order_launch(const int32_t* seqlens, int B, int32_t* order, void* stream);
+int mxfa_kvcache_attention_ordered_launch(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_table, const int32_t* seqlens,
+                                          const int32_t* length_order, void* out, float* lse, void* workspace,
+                                          size_t workspace_bytes, unsigned int* counters, int B, int Sq, int HQ,
+                                          int HKV, int D, int PS, int BTW, int num_pages, int append_len,
+                                          int num_splits, int chunk_len, int causal, int bf16, float scale,
+                                          int kv_fp8, float k_scale, float v_scale, void* stream);
 
 /* mxfa_kvcache_attention_launch with the append fused into the same launch:
  * the append of reference.py:108-122 (what mxfa_kv_append_launch does) plus

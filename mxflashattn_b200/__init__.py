@@ -8,7 +8,7 @@ record, validation and policy objects.
 """
 
 from .accuracy import ErrorSummary, summarize_error
-from .api import flash_attn_func, flash_attn_varlen_func, flash_attn_with_kvcache
+from .api import flash_attn_func, flash_attn_varlen_func, flash_attn_with_kvcache, kvcache_length_order
 from .dispatch import BACKEND_LABEL, BackendUnavailableError, DispatchInfo, get_last_dispatch_info
 from .policy import AdaptiveDispatchPolicy, DispatchDecision, DispatchPolicyConfig, WorkloadShape
 
@@ -20,6 +20,7 @@ __all__ = [
     "flash_attn_varlen_func",
     "flash_attn_with_kvcache",
     "get_last_dispatch_info",
+    "kvcache_length_order",
     "AdaptiveDispatchPolicy",
     "DispatchDecision",
     "DispatchPolicyConfig",

@@ -23,6 +23,7 @@ FLAG_PAGE_OUT_OF_RANGE = 0x1
 FLAG_TABLE_TOO_NARROW = 0x2
 FLAG_WAIT_TIMEOUT = 0x4
 FLAG_DENSE_OVERFLOW = 0x8
+FLAG_BAD_ORDER = 0x10
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -49,6 +50,10 @@ SIGNATURES = {
     "mxfa_kvcache_attention_fp8_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _f, _f, _f, _vp]),
+    "mxfa_kvcache_length_order_launch": (_i, [_vp, _i, _vp, _vp]),
+    "mxfa_kvcache_attention_ordered_launch": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _i, _i, _f, _i, _f, _f, _vp]),
     "mxfa_kvcache_append_attention_launch": (
         _i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _i, _i, _i, _f, _vp]),

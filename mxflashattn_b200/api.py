@@ -139,6 +139,7 @@ def flash_attn_with_kvcache(
     k_scale: float | None = None,
     v_scale: float | None = None,
     out: torch.Tensor | None = None,
+    length_order: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Paged or dense KV-cache attention with optional append (api.py:151-286).
 
@@ -151,7 +152,11 @@ def flash_attn_with_kvcache(
     and ``v_cache * v_scale`` (default 1.0), and appended ``k``/``v`` must
     then already be e4m3 with the same scales.  ``out`` (contiguous, q's
     shape, dtype and device) receives the result instead of a new tensor and
-    is returned.
+    is returned.  ``length_order`` (int32 [B] on q's device, from
+    ``kvcache_length_order(cache_seqlens)``, computed once per step and
+    passed to every layer) schedules the sequences longest first without the
+    ranking each launch otherwise does; it only orders the work, so the
+    result is the same with or without it.
     """
     validate_softmax_scale(softmax_scale)
     if rotary_cos is not None or rotary_sin is not None:
@@ -216,15 +221,40 @@ def flash_attn_with_kvcache(
     if out is not None and (not isinstance(out, torch.Tensor) or out.shape != q.shape or out.dtype != q.dtype
                             or out.device != q.device or not out.is_contiguous()):
         raise ValueError("out must be a contiguous tensor with q's shape, dtype and device")
+    if length_order is not None and (not isinstance(length_order, torch.Tensor) or length_order.dtype != torch.int32
+                                     or length_order.shape != (q.shape[0],) or length_order.device != q.device):
+        raise ValueError("length_order must be an int32 tensor with one entry per batch item on q's device")
     if os.getenv("MXFLASHATTN_STRICT_VALIDATION", "0") == "1":
         _strict_kvcache_checks(k_cache, k, cache_seqlens, block_table)
     args = (q, k_cache, v_cache, k, v, cache_seqlens, block_table, _resolved_scale(q.shape[-1], softmax_scale),
             causal)
-    if fp8_cache or out is not None:
+    if fp8_cache or out is not None or length_order is not None:
         args += (1.0 if k_scale is None else float(k_scale), 1.0 if v_scale is None else float(v_scale))
-    if out is not None:
+    if out is not None or length_order is not None:
         args += (out,)
+    if length_order is not None:
+        args += (length_order,)
     return dispatch("flash_attn_with_kvcache", q, args)
+
+
+def kvcache_length_order(cache_seqlens: torch.Tensor) -> torch.Tensor | None:
+    """The batch's longest-first order for ``flash_attn_with_kvcache(..., length_order=)``.
+
+    No reference counterpart (an extension of this package).  One small
+    kernel writes int32 [B] (order[rank] = sequence index, ties by index) on
+    the device; call it once per decode step, after the lengths are final,
+    and pass the result to every layer.  None for batches of one or of more
+    than 512 sequences, which need no order.
+    """
+    if not isinstance(cache_seqlens, torch.Tensor):
+        raise TypeError("cache_seqlens must be a torch.Tensor")
+    if cache_seqlens.ndim != 1 or cache_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError("cache_seqlens must be a one-dimensional int32 or int64 tensor")
+    if cache_seqlens.device.type != "cuda":
+        raise ValueError("cache_seqlens must be on a CUDA device")
+    from . import backend
+
+    return backend.kvcache_length_order(cache_seqlens)
 
 
 _FP8 = getattr(torch, "float8_e4m3fn", None)

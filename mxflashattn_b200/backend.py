@@ -166,10 +166,28 @@ def split_counters(device, stream_handle: int, nbytes: int):
     return buf
 
 
+def kvcache_length_order(cache_seqlens):
+    """Longest-first order of the batch (int32 [B]: order[rank] = sequence), for ``length_order=``.
+
+    Computed on the device (``mxfa_kvcache_length_order_launch``) once per
+    step and passed to every layer's ``kvcache_attention``, it replaces the
+    ranking each CTA otherwise does on every layer.  Batches of one or of more
+    than 512 sequences need none (None is returned)."""
+    seq = _i32(cache_seqlens)
+    B = seq.shape[0]
+    if B <= 1 or B > 512:
+        return None
+    order = torch.empty((B,), device=seq.device, dtype=torch.int32)
+    with _on(seq):
+        rc = _L().mxfa_kvcache_length_order_launch(seq.data_ptr(), B, order.data_ptr(), _stream(seq))
+    _lib.check(rc, "mxfa_kvcache_length_order_launch")
+    return order
+
+
 def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal, *,
                       append_len: int = 0, return_lse: bool = False, num_splits: int = 0, chunk_len: int = 0,
                       out=None, k_new=None, v_new=None, single_launch: bool = True, k_scale: float = 1.0,
-                      v_scale: float = 1.0):
+                      v_scale: float = 1.0, length_order=None):
     """Attention of q [B, Sq, HQ, D] over the cached tokens (+ ``append_len``).
 
     ``cache_seqlens`` holds the lengths before the append.  Without
@@ -180,6 +198,8 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
     launch (the last split CTA of each unit merges) unless ``single_launch``
     is False, which keeps the separate combine kernel.  ``torch.float8_e4m3fn``
     caches attend to ``k_cache * k_scale`` and ``v_cache * v_scale``.
+    ``length_order`` (from ``kvcache_length_order``) schedules the sequences
+    without the per-CTA ranking; it is ignored by the fused append.
     """
     B, Sq, HQ, D = q.shape
     q = _contig(q)
@@ -211,7 +231,18 @@ def kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_s
         counters = None
         if num_splits > 1 and single_launch:
             counters = split_counters(q.device, stream, int(lib.mxfa_split_counter_bytes(B, Sq, HQ, HKV)))
-        if _is_fp8(k_cache):
+        if length_order is not None and k_new is None:
+            order = _i32(length_order)
+            if order.shape != (B,) or order.device != q.device:
+                raise ValueError(f"length_order must be int32 [{B}] on {q.device}")
+            fp8 = _is_fp8(k_cache)
+            name = "mxfa_kvcache_attention_ordered_launch"
+            rc = lib.mxfa_kvcache_attention_ordered_launch(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(bt), seq.data_ptr(), order.data_ptr(),
+                out.data_ptr(), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, _lib.ptr(counters), B, Sq, HQ, HKV, D, PS,
+                btw, pages, int(append_len), num_splits, chunk_len, int(bool(causal)), _bf16(q),
+                float(softmax_scale), int(fp8), float(k_scale), float(v_scale), stream)
+        elif _is_fp8(k_cache):
             if k_new is not None:
                 raise ValueError("the fused append does not take float8_e4m3fn rows; append with kv_append first")
             name = "mxfa_kvcache_attention_fp8_launch"
@@ -288,13 +319,15 @@ def seqlens_add_(cache_seqlens: torch.Tensor, delta: int) -> None:
 
 
 def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_table, softmax_scale, causal,
-                            k_scale: float = 1.0, v_scale: float = 1.0, out=None):
+                            k_scale: float = 1.0, v_scale: float = 1.0, out=None, length_order=None):
     """``flash_attn_with_kvcache`` semantics of the reference (reference.py:88-139).
 
     Appends ``k``/``v`` (when given) at the current lengths, attends over the
     grown cache, then advances ``cache_seqlens`` in place -- all on the
     current stream, with no host synchronisation.  ``out`` (optional, q's
-    shape and dtype, contiguous) receives the result.
+    shape and dtype, contiguous) receives the result.  ``length_order``
+    (optional, from ``kvcache_length_order``) schedules the sequences without
+    the per-launch ranking.
     """
     if q.shape[1] == 0:
         if k is not None:
@@ -313,7 +346,8 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, block_tabl
         kv_append(k_cache, v_cache, k, v, cache_seqlens, block_table)
         append_len = k.shape[1]
     out = kvcache_attention(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, causal,
-                            append_len=append_len, k_scale=k_scale, v_scale=v_scale, out=out)
+                            append_len=append_len, k_scale=k_scale, v_scale=v_scale, out=out,
+                            length_order=length_order)
     if k is not None:
         seqlens_add_(cache_seqlens, append_len)
     return out

@@ -491,7 +491,7 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
                                   int PS, int BTW, int num_pages, int append_len, int num_splits, int chunk_len,
                                   int causal, int bf16, float scale, const void* k_new, const void* v_new,
                                   unsigned* counters, void* stream, bool kv_fp8 = false, float k_scale = 1.f,
-                                  float v_scale = 1.f) {
+                                  float v_scale = 1.f, const int32_t* order = nullptr) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B < 0 || Sq < 0 || HQ <= 0 || HKV <= 0 || HQ % HKV != 0)
     return fail(MXFA_ERR_INVALID, "bad head / batch geometry (B=%d Sq=%d HQ=%d HKV=%d)", B, Sq, HQ, HKV);
@@ -523,6 +523,7 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   p.v_scale = kv_fp8 ? v_scale : 1.f;
   p.k_new = k_new;
   p.v_new = v_new;
+  p.order = order;
   const int max_len = block_table ? BTW * PS : PS;
   if (num_splits <= 0 || chunk_len <= 0) {
     mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
@@ -613,6 +614,39 @@ int mxfa_kvcache_append_attention_launch(const void* q, void* k_cache, void* v_c
   return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes,
                                 B, Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal,
                                 bf16, scale, k_new, v_new, counters, stream);
+}
+
+int mxfa_kvcache_length_order_launch(const int32_t* seqlens, int B, int32_t* order, void* stream) {
+  if (B <= 0) return MXFA_OK;
+  if (B > kRankMaxBatch) return fail(MXFA_ERR_UNSUPPORTED, "length order covers up to %d sequences", kRankMaxBatch);
+  if (seqlens == nullptr || order == nullptr) return fail(MXFA_ERR_INVALID, "null pointer");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kRankMaxBatch);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, length_order_kernel, seqlens, B, order);
+  if (e != cudaSuccess) return fail(MXFA_ERR_CUDA, "length_order_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("length_order_kernel");
+}
+
+int mxfa_kvcache_attention_ordered_launch(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_table, const int32_t* seqlens,
+                                          const int32_t* length_order, void* out, float* lse, void* workspace,
+                                          size_t workspace_bytes, unsigned* counters, int B, int Sq, int HQ, int HKV,
+                                          int D, int PS, int BTW, int num_pages, int append_len, int num_splits,
+                                          int chunk_len, int causal, int bf16, float scale, int kv_fp8,
+                                          float k_scale, float v_scale, void* stream) {
+  if (kv_fp8 && (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale)))
+    return fail(MXFA_ERR_INVALID, "k_scale / v_scale must be positive and finite");
+  return kvcache_attention_impl(q, k_cache, v_cache, block_table, seqlens, out, lse, workspace, workspace_bytes, B,
+                                Sq, HQ, HKV, D, PS, BTW, num_pages, append_len, num_splits, chunk_len, causal, bf16,
+                                scale, nullptr, nullptr, counters, stream, kv_fp8 != 0, k_scale, v_scale,
+                                length_order);
 }
 
 // ------------------------------------------------ context-parallel exchange

@@ -70,6 +70,12 @@ struct DecodeParams {
   const unsigned long long* cp_bufs;  // [cp_world] exchange-buffer bases; [cp_rank] is local
   int cp_rank, cp_world;
   int cp_merge;
+  // Length order (optional, 1 < B <= kRankMaxBatch): order[y] is the
+  // sequence that grid row y runs, longest first, as length_order_kernel
+  // writes it once per step for every layer.  Without it each CTA ranks the
+  // lengths itself.  Only the schedule depends on it: lengths are always
+  // read from seqlens.
+  const int* order;
   // Fused append (optional): append_len new tokens per sequence, [B, append_len, HKV, D],
   // written into the cache by the CTA that reads them (one query-row group only).
   const void* k_new;
@@ -468,8 +474,15 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int b = blockIdx.y;
-  int cached_len;
-  if (p.B > 1 && p.B <= kRankMaxBatch) {
+  int cached_len = 0;
+  bool have_len = false;
+  if (p.order != nullptr && p.B > 1 && p.B <= kRankMaxBatch) {
+    b = p.order[blockIdx.y];
+    if (b < 0 || b >= p.B) {  // not a permutation of the batch: run row y's own sequence
+      raise_flag(MXFA_FLAG_BAD_ORDER);
+      b = blockIdx.y;
+    }
+  } else if (p.B > 1 && p.B <= kRankMaxBatch) {
     // Rank every sequence by length (ties by index) and take the one whose
     // rank is this block's y.  Each sequence gets one packed key -- length in
     // the high bits, reversed index in the low 9 -- so keys are unique and a
@@ -507,19 +520,16 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
     __syncthreads();
     b = s_seq;
     cached_len = s_len;
-  } else {
-    cached_len = p.seqlens[b];
+    have_len = true;
   }
 
-  const int total_len = cached_len + p.append_len;
   // split mode (partials written for a combine) whenever a workspace is given;
   // chunk z then covers [z*c_len, (z+1)*c_len) exactly as the reference's split
-  int lo = 0, hi = total_len;
-  if (p.ows != nullptr) {
-    lo = z * p.c_len;
-    hi = min(lo + p.c_len, total_len);
-  }
+  const int lo = p.ows != nullptr ? z * p.c_len : 0;
   const int tile0 = (lo / kTileTok) * kTileTok;
+  if (!have_len) cached_len = p.seqlens[b];
+  const int total_len = cached_len + p.append_len;
+  const int hi = p.ows != nullptr ? min(lo + p.c_len, total_len) : total_len;
   const int ntiles = (hi > lo) ? (hi - tile0 + kTileTok - 1) / kTileTok : 0;
 
   // The producer's first block-table reads go out now, so their latency
@@ -1229,6 +1239,26 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
     const size_t dst = ((static_cast<size_t>(phys) * p.PS + slot) * p.HKV + h) * p.row_bytes + c * 16;
     *reinterpret_cast<uint4*>(p.k_cache + dst) = *reinterpret_cast<const uint4*>(p.k_new + src);
     *reinterpret_cast<uint4*>(p.v_cache + dst) = *reinterpret_cast<const uint4*>(p.v_new + src);
+  }
+}
+
+// Longest-first order of a batch (ties by index), the permutation the decode
+// kernel otherwise derives in every CTA: one block, thread i ranks sequence i
+// against all others with the same packed key (length in the high bits,
+// reversed index in the low 9) and writes order[rank] = i.
+__global__ void __launch_bounds__(kRankMaxBatch) length_order_kernel(const int* __restrict__ seqlens, int B,
+                                                                     int* __restrict__ order) {
+  __shared__ int keys[kRankMaxBatch];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int i = threadIdx.x;
+  int key = -1;
+  if (i < B) key = (min(max(seqlens[i], 0), (1 << 22) - 1) << 9) | (kRankMaxBatch - 1 - i);
+  keys[i] = key;
+  __syncthreads();
+  if (i < B) {
+    int rank = 0;
+    for (int j = 0; j < B; ++j) rank += keys[j] > key;
+    order[rank] = i;
   }
 }
 

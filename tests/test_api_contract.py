@@ -260,3 +260,32 @@ def test_out_buffer_is_validated_and_passed_to_the_backend(monkeypatch):
     # without `out` the backend receives the reference's nine positional arguments
     flash_attn_with_kvcache(q, k, v, cache_seqlens=sl)
     assert len(calls[1]) == 9
+
+
+def test_length_order_is_validated_and_passed_to_the_backend(monkeypatch):
+    calls = []
+    ext = SimpleNamespace(is_available=lambda: True,
+                          flash_attn_with_kvcache=lambda *args: calls.append(args) or args[0])
+    monkeypatch.setattr(dispatch, "_native_extension", lambda: ext)
+    monkeypatch.setattr(dispatch, "native_unavailable_reason", lambda tensor, op: None)
+    q, k, v = tensors()
+    sl = torch.tensor([3], dtype=torch.int32)
+    for bad in (torch.zeros(1, dtype=torch.int64), torch.zeros(2, dtype=torch.int32), [0]):
+        with pytest.raises(ValueError, match="length_order must be"):
+            flash_attn_with_kvcache(q, k, v, cache_seqlens=sl, length_order=bad)
+    assert not calls
+    order = torch.zeros(1, dtype=torch.int32)
+    flash_attn_with_kvcache(q, k, v, cache_seqlens=sl, length_order=order)
+    # scales, out (None) and the order follow the reference's nine positional arguments
+    assert len(calls[0]) == 13 and calls[0][-2] is None and calls[0][-1] is order
+
+
+def test_length_order_helper_guards():
+    from mxflashattn_b200 import kvcache_length_order
+
+    with pytest.raises(TypeError, match="torch.Tensor"):
+        kvcache_length_order([1, 2])
+    with pytest.raises(ValueError, match="one-dimensional"):
+        kvcache_length_order(torch.zeros(2, 2, dtype=torch.int32))
+    with pytest.raises(ValueError, match="CUDA device"):
+        kvcache_length_order(torch.zeros(4, dtype=torch.int32))
