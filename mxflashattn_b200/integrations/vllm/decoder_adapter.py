@@ -21,7 +21,7 @@ from typing import Any
 
 import torch
 
-from mxflashattn_b200 import flash_attn_with_kvcache
+from mxflashattn_b200 import flash_attn_with_kvcache, kvcache_length_order
 
 STRICT_LAYOUT = os.getenv("MXFLASHATTN_STRICT_LAYOUT", "0") == "1"
 _REQUIRED = ("num_actual_tokens", "max_query_len", "query_start_loc", "max_seq_len", "seq_lens", "block_table",
@@ -104,6 +104,27 @@ def fast_layout(query: torch.Tensor, kv_cache: torch.Tensor, attn_metadata: Any)
     )
 
 
+def _step_length_order(attn_metadata, cache_seqlens: torch.Tensor):
+    """The batch's longest-first order, computed by the step's first layer and reused by the others.
+
+    vLLM hands one metadata object per step to every attention layer, so the
+    order (one small kernel) is kept on it.  The order only schedules the
+    work: a metadata object reused with other lengths costs speed, never
+    correctness.  Objects that take no new attributes recompute per layer.
+    None off the GPU (the order is a launch option of the CUDA backend).
+    """
+    if not cache_seqlens.is_cuda:
+        return None
+    order = getattr(attn_metadata, "_mxfa_length_order", None)
+    if order is None or order.shape[0] != cache_seqlens.shape[0] or order.device != cache_seqlens.device:
+        order = kvcache_length_order(cache_seqlens)
+        try:
+            attn_metadata._mxfa_length_order = order
+        except (AttributeError, TypeError):  # frozen or slotted metadata
+            pass
+    return order
+
+
 def _as_device_i32(t: torch.Tensor, device) -> torch.Tensor:
     # vLLM already keeps these int32 on the device; convert only when it does not
     return t if (t.device == device and t.dtype == torch.int32) else t.to(device=device, dtype=torch.int32)
@@ -148,11 +169,11 @@ def decode_forward(
         key_cache, value_cache = kv_cache.unbind(0)
         n = int(attn_metadata.num_actual_tokens)
         q = query[:n].reshape(n, 1, query.shape[1], query.shape[2])
-        seq_lens = attn_metadata.seq_lens.reshape(-1)  # capture metadata may be [1, batch]
+        seq_lens = _as_device_i32(attn_metadata.seq_lens.reshape(-1), query.device)  # capture metadata may be [1, batch]
         result = flash_attn_with_kvcache(
-            q, key_cache, value_cache, cache_seqlens=_as_device_i32(seq_lens, query.device),
+            q, key_cache, value_cache, cache_seqlens=seq_lens,
             block_table=_as_device_i32(attn_metadata.block_table, query.device), softmax_scale=softmax_scale,
-            causal=causal)
+            causal=causal, length_order=_step_length_order(attn_metadata, seq_lens))
         return result.reshape(n, -1), None
     layout = inspect_layout(query, kv_cache, attn_metadata) if STRICT_LAYOUT else fast_layout(
         query, kv_cache, attn_metadata)
@@ -169,10 +190,11 @@ def decode_forward(
     key_cache, value_cache = kv_cache.unbind(0)
     batch = layout.batch_size
     q = query[: layout.num_actual_tokens].reshape(batch, 1, query.shape[1], query.shape[2])
+    seq_lens = _as_device_i32(attn_metadata.seq_lens, query.device)
     result = flash_attn_with_kvcache(
-        q, key_cache, value_cache, cache_seqlens=_as_device_i32(attn_metadata.seq_lens, query.device),
+        q, key_cache, value_cache, cache_seqlens=seq_lens,
         block_table=_as_device_i32(attn_metadata.block_table, query.device), softmax_scale=softmax_scale,
-        causal=causal)
+        causal=causal, length_order=_step_length_order(attn_metadata, seq_lens))
     return result.reshape(layout.num_actual_tokens, -1), layout
 
 
@@ -206,5 +228,6 @@ def _decode_forward_graph(query, kv_cache, attn_metadata, *, softmax_scale: floa
     if cache_seqlens.numel() != batch or block_table.shape[0] != batch:
         raise DecoderAdapterBlocked("decode_metadata_batch_mismatch")
     result = flash_attn_with_kvcache(q, key_cache, value_cache, cache_seqlens=cache_seqlens,
-                                     block_table=block_table, softmax_scale=softmax_scale, causal=causal)
+                                     block_table=block_table, softmax_scale=softmax_scale, causal=causal,
+                                     length_order=_step_length_order(attn_metadata, cache_seqlens))
     return result.reshape(q.shape[0] * q.shape[1], -1), None

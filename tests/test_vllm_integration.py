@@ -228,3 +228,25 @@ def test_smoke_generate_compare_and_event_counts(tmp_path):
     log.write_text('{"path": "cuda_sm100"}\n{"path": "cuda_sm100"}\n{"path": "vendor_prefill_or_blocked"}\n')
     assert sg.count_events(log) == {"cuda_sm100": 2, "vendor_prefill_or_blocked": 1}
     assert sg.count_events(tmp_path / "missing.jsonl") == {}
+
+
+def test_length_order_is_computed_once_per_step_metadata(monkeypatch):
+    """Every layer of a step gets the metadata object the first layer saw: one order kernel per step."""
+    from types import SimpleNamespace
+
+    made = []
+
+    def fake_order(seqlens):
+        made.append(seqlens)
+        return SimpleNamespace(shape=seqlens.shape, device=seqlens.device)
+
+    monkeypatch.setattr(decoder_adapter, "kvcache_length_order", fake_order)
+    seq = SimpleNamespace(is_cuda=True, shape=(2,), device="cuda:0")
+    md = SimpleNamespace()
+    first = decoder_adapter._step_length_order(md, seq)
+    assert decoder_adapter._step_length_order(md, seq) is first and len(made) == 1
+    # another batch size on the same object: recomputed
+    decoder_adapter._step_length_order(md, SimpleNamespace(is_cuda=True, shape=(3,), device="cuda:0"))
+    assert len(made) == 2
+    # host tensors: no order
+    assert decoder_adapter._step_length_order(SimpleNamespace(), torch.tensor([1, 2])) is None
