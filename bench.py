@@ -56,7 +56,7 @@ PREFILL_LENS = "15000,1024,512,37"
 # launch of the default workload (batch 128, seed 2026), taken once by ncu
 # on one launch of this exact command; reported as a profile value
 # (`traffic_source`), not measured by the run that prints it.
-NCU_TRAFFIC_BYTES = {(128, 2026): 381.832192e6}
+NCU_TRAFFIC_BYTES = {(128, 2026): 381.349120e6}
 METRIC = "decode-attn KV HBM GB/s & tok/s (Qwen3-4B shape, b128) at 1/2/4/8 B200"
 WORKLOAD = "qwen3-4b paged decode attention, b128, 36 layers (config 2)"
 REF_PACKAGE_DIR = os.path.join(REPO, "baseline", "_ref")
