@@ -1071,6 +1071,7 @@ __global__ void __launch_bounds__(kDecThreads, DecodeCfg<HD, NT, kFp8>::kCtasPer
             const int R = (b * p.Sq + rr / p.GQ) * p.HQ + h;
             cp_merge_row_call<T, HD>(recs, rows_all, R, p.cp_world, lane, static_cast<T*>(p.out), p.lse, tag, t0);
           }
+          __syncwarp();  // lanes leave their per-word waits at different times
           named_barrier_sync(1, kDecConsumerWarps * 32);
           if (tid == 0) {
             __threadfence();
@@ -1182,6 +1183,7 @@ __global__ void __launch_bounds__(128) cp_merge_kernel(unsigned char* buf, T* __
   if (r < rows)
     cp_merge_row<T, HD>(reinterpret_cast<const uint64_t*>(buf + lay.records + (epoch & 1u) * lay.record_half), rows,
                         r, world, lane, out, lse, epoch + 1u, global_timer_ns());
+  __syncwarp();  // lanes leave their per-word waits at different times
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
