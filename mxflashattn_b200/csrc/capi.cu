@@ -958,6 +958,37 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
   return check_launch("seqlens_add_kernel");
 }
 
+// Work counter of the persistent prefill kernel, one per (device, stream):
+// launches on one stream run in order, so they can share it (each launch
+// leaves it zero).  Allocated on a stream's first launch outside graph
+// capture; a launch that finds none (first launch on a stream while it is
+// being captured, or too many streams) runs the fixed per-CTA shares.
+static unsigned* prefill_sched_counter(cudaStream_t st) {
+  static std::mutex mu;
+  static std::unordered_map<unsigned long long, unsigned*> counters;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  const unsigned long long key = (static_cast<unsigned long long>(dev) << 56) ^ reinterpret_cast<uintptr_t>(st);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = counters.find(key);
+  if (it != counters.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  if (counters.size() >= 4096) return nullptr;
+  void* ptr = nullptr;
+  if (cudaMalloc(&ptr, 2 * sizeof(unsigned)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemset(ptr, 0, 2 * sizeof(unsigned)) != cudaSuccess) {
+    cudaFree(ptr);
+    cudaGetLastError();
+    return nullptr;
+  }
+  counters.emplace(key, static_cast<unsigned*>(ptr));
+  return static_cast<unsigned*>(ptr);
+}
+
 static int varlen_fwd_impl(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
                            void* out, float* lse, int B, int max_q, int max_k, int total_q, int total_k, int HQ,
                            int HKV, int D, int causal, int bf16, float scale, void* stream, bool exact) {
@@ -971,7 +1002,9 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
     return fail(MXFA_ERR_INVALID, "dense layout needs total_q = B*max_q and total_k = B*max_k");
   if (!q || !k || !v || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
-  if (HQ > 65535 || B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "grid too large");
+  // work items are numbered (query tile * B + sequence) * HQ + head
+  if (static_cast<long long>((max_q + kTcRows - 1) / kTcRows) * B * HQ > INT_MAX)
+    return fail(MXFA_ERR_UNSUPPORTED, "too many query tiles");
   PrefillParams p{};
   p.q = q;
   p.k = k;
@@ -989,6 +1022,7 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  p.sched = prefill_sched_counter(st);
   // TMA maps cover exactly the token rows of q and k/v: boxes reaching past
   // the last row read zeros instead of memory beyond the tensors
   int dev = 0;
@@ -1006,7 +1040,9 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   const CUtensorMap& mq = maps.q;
   const CUtensorMap& mk = maps.k;
   const CUtensorMap& mv = maps.v;
-  dim3 grid(HQ, B, (max_q + kTcRows - 1) / kTcRows);
+  // persistent: one CTA per SM (fewer when there are fewer query tiles)
+  const long long tiles = static_cast<long long>((max_q + kTcRows - 1) / kTcRows) * B * HQ;
+  dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
   auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done, int threads) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;
     kern<<<grid, threads, smem, st>>>(p, mq, mk, mv);
