@@ -298,3 +298,41 @@ def test_cached_tensor_maps_follow_the_shape_at_the_same_address(cuda_device):
         ref = oracle.attention_varlen(big.q[:n], big.k[:n], big.v[:n], np.array([0, n], np.int32),
                                       np.array([0, n], np.int32), softmax_scale=big.softmax_scale, causal=True)
         assert_close_out(host(out), ref, "bf16", f"rows {n}")
+
+
+def test_work_counter_and_fixed_shares_give_the_same_bits(cuda_device):
+    """The persistent kernel takes query tiles from a per-stream work counter, or, when a stream's first launch
+    happens during graph capture (no counter can be allocated then), from fixed per-CTA shares.  Only the
+    schedule differs: a captured first launch on a fresh stream, its replays, and later eager launches on that
+    stream (which then have a counter, left zero by each launch) all give the same bits."""
+    import torch
+
+    from mxflashattn_b200 import backend
+
+    case = syn.varlen_case(91, q_lens=[3000, 700, 129, 5], q_heads=8, kv_heads=2, head_dim=128, dtype="bf16",
+                           causal=True)
+    q, k, v, cu_q, cu_k = _dev(case, cuda_device)
+
+    def call():
+        return backend.flash_attn_varlen_func(q, k, v, cu_q, cu_k, 3000, 3000, True, case.softmax_scale)
+
+    call()  # kernel attributes and tensor maps set up outside the capture, on another stream
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(cuda_device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        captured = call()
+    outs = []
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            graph.replay()
+            outs.append(captured.clone())
+        for _ in range(3):
+            outs.append(call())
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = oracle.attention_varlen(case.q, case.k, case.v, case.cu_q, case.cu_k, causal=True)
+    abs_v = oracle.attention_varlen(case.q, case.k, np.abs(case.v), case.cu_q, case.cu_k, causal=True)
+    assert_close_out(host(outs[0]), ref, "bf16", "fixed shares / work counter", extra=p_rounding_bound("bf16", abs_v))
+    del graph
