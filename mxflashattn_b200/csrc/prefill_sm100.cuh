@@ -895,11 +895,11 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
         } else {
           // diagonal tile: a rolled loop over 16-column chunks keeps this
           // rarely taken path out of the way of the unrolled one
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < kTcKeys; c += 16) {
             uint32_t raw[16];
             tmem_ld16(sbuf + c, raw);
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float v = __uint_as_float(raw[i]);
               const bool vis = key0 + c + i < vis_end;
@@ -939,11 +939,11 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
           }
           tc_fence_after();
           const float alpha = grow ? fast_exp2(m_in - m_j) : 1.f;  // 0 when m_in = -inf
-  #pragma unroll
+#pragma unroll
           for (int c = 0; c < HD; c += 32) {
             uint32_t o[32];
             tmem_ld32(o_base + c, o);
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st32(o_base + c, o);
           }
@@ -957,14 +957,14 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
           // 64-key halves read at once; per 16-key chunk, P_hi then P_lo in the
           // chunk's own (already read) columns, stored 32 columns at a time
           float r0 = 0.f, r1 = 0.f;
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < kTcKeys; c += 64) {
             uint32_t raw[64];
             tmem_ld64(sbuf + c, raw);
-  #pragma unroll
+#pragma unroll
             for (int qq = 0; qq < 2; ++qq) {
               uint32_t packed[32];
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 32; i += 2) {
                 const float p0 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i]), sc, neg_m));
                 const float p1 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i + 1]), sc, neg_m));
@@ -983,12 +983,12 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
         } else if constexpr (kExactP) {
           // diagonal tile, 16-key chunks: P_hi and P_lo land in the chunk's own (already read) columns
           const bool live = m_j != -INFINITY;
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < kTcKeys; c += 16) {
             uint32_t raw[16];
             tmem_ld16(sbuf + c, raw);
             uint32_t packed[16];
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 16; i += 2) {
               const bool v0 = live && (all_full || key0 + c + i < vis_end);
               const bool v1 = live && (all_full || key0 + c + i + 1 < vis_end);
@@ -1030,12 +1030,12 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
           rs = a + bb;
         } else {
           const bool live = m_j != -INFINITY;
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < kTcKeys; c += 16) {
             uint32_t raw[16];
             tmem_ld16(sbuf + c, raw);
             uint32_t packed[8];
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 16; i += 2) {
               const bool v0 = live && key0 + c + i < vis_end;
               const bool v1 = live && key0 + c + i + 1 < vis_end;
