@@ -434,6 +434,33 @@ int launch_packed_combine(const float* ows, const float* mdws, float* packed, in
   return check_launch("split_combine_kernel(packed)");
 }
 
+// Process-unique id of the calling thread's current context (0 if none or
+// the driver cannot say).  Context ids are never reused within a process,
+// unlike context handles.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
 }  // namespace
 }  // namespace mxfa
 
@@ -958,17 +985,31 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
   return check_launch("seqlens_add_kernel");
 }
 
-// Work counter of the persistent prefill kernel, one per (device, stream):
+// Work counter of the persistent prefill kernel, one per (context, stream):
 // launches on one stream run in order, so they can share it (each launch
 // leaves it zero).  Allocated on a stream's first launch outside graph
 // capture; a launch that finds none (first launch on a stream while it is
-// being captured, or too many streams) runs the fixed per-CTA shares.
+// being captured, no context id, or too many streams) runs the fixed per-CTA
+// shares.  Keyed by the context's id, so a device whose context was torn
+// down and re-created gets a new counter instead of a freed one.
 static unsigned* prefill_sched_counter(cudaStream_t st) {
+  struct Key {
+    unsigned long long ctx;
+    uintptr_t stream;
+    bool operator==(const Key& o) const { return ctx == o.ctx && stream == o.stream; }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const { return std::hash<unsigned long long>()(k.ctx * 0x9E3779B97F4A7C15ull ^ k.stream); }
+  };
   static std::mutex mu;
-  static std::unordered_map<unsigned long long, unsigned*> counters;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  const unsigned long long key = (static_cast<unsigned long long>(dev) << 56) ^ reinterpret_cast<uintptr_t>(st);
+  static std::unordered_map<Key, unsigned*, KeyHash> counters;
+  unsigned long long ctx = current_context_id();
+  if (ctx == 0) {  // no context current yet (a first call from a bare host): create the device's primary one
+    cudaFree(nullptr);
+    ctx = current_context_id();
+    if (ctx == 0) return nullptr;
+  }
+  const Key key{ctx, reinterpret_cast<uintptr_t>(st)};
   std::lock_guard<std::mutex> lock(mu);
   auto it = counters.find(key);
   if (it != counters.end()) return it->second;
@@ -1103,33 +1144,6 @@ namespace mxfa {
 namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[MXFA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
-
-// Process-unique id of the calling thread's current context (0 if none or
-// the driver cannot say).  Context ids are never reused within a process,
-// unlike context handles.
-unsigned long long current_context_id() {
-  using GetCurrent = CUresult (*)(CUcontext*);
-  using GetId = CUresult (*)(CUcontext, unsigned long long*);
-  static GetCurrent get_current = nullptr;
-  static GetId get_id = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_current = reinterpret_cast<GetCurrent>(p);
-    p = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_id = reinterpret_cast<GetId>(p);
-  });
-  if (get_current == nullptr || get_id == nullptr) return 0;
-  CUcontext ctx = nullptr;
-  unsigned long long id = 0;
-  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
-  return id;
-}
 
 int noalloc_scratch(float** out) {
   static float* addr[64] = {};
