@@ -556,8 +556,10 @@ struct TcWalk {
   }
 };
 
-// Persistent: one CTA per SM walks its share of the work list.  The roles
-// keep their own positions in one stream of key tiles across items (tile t
+// Persistent: one CTA per SM takes query tiles (items) from the work list,
+// from the shared work counter when the launch has one, else its fixed
+// share.  The roles keep their own positions in one stream of key tiles
+// across items (tile t
 // uses K/V stage t%3 and S/P buffer t%3, barrier phases follow t), so the
 // next item's Q and first K tiles load, and its first score products run,
 // while this item's last tiles and epilogue finish.  The producer publishes
