@@ -333,13 +333,8 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
  *   cu_q, cu_k int32 [B + 1] device arrays (or NULL for dense)
  *   out [Tq, HQ, D]; lse optional f32 [Tq, HQ]
  *   total_q = Tq, total_k = Tk: the row counts of q and k/v (dense: B*max_q, B*max_k)
- * max_q must bound every q length (it sizes the work list).  Runs on the
- * tcgen05 tensor cores (sm_100a), operands staged by TMA, accumulators in
- * TMEM, as a persistent kernel (one CTA per SM) that takes query tiles from a
- * work counter.  The library keeps one two-word counter per device and
- * stream, allocated (8 bytes) on the stream's first launch outside graph
- * capture and left zero by every launch; a launch without one (the first on
- * a stream while it is captured) splits the tiles in fixed shares instead. */
+ * max_q must bound every q length (it sizes the grid).  Runs on the tcgen05
+ * tensor cores (sm_100a), operands staged by TMA, accumulators in TMEM. */
 int mxfa_varlen_fwd_launch(const void* q, const void* k, const void* v, const int32_t* cu_q,
                            const int32_t* cu_k, void* out, float* lse, int B, int max_q, int max_k,
                            int total_q, int total_k, int HQ, int HKV, int D, int causal, int bf16,

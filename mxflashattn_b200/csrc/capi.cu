@@ -434,33 +434,6 @@ int launch_packed_combine(const float* ows, const float* mdws, float* packed, in
   return check_launch("split_combine_kernel(packed)");
 }
 
-// Process-unique id of the calling thread's current context (0 if none or
-// the driver cannot say).  Context ids are never reused within a process,
-// unlike context handles.
-unsigned long long current_context_id() {
-  using GetCurrent = CUresult (*)(CUcontext*);
-  using GetId = CUresult (*)(CUcontext, unsigned long long*);
-  static GetCurrent get_current = nullptr;
-  static GetId get_id = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_current = reinterpret_cast<GetCurrent>(p);
-    p = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_id = reinterpret_cast<GetId>(p);
-  });
-  if (get_current == nullptr || get_id == nullptr) return 0;
-  CUcontext ctx = nullptr;
-  unsigned long long id = 0;
-  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
-  return id;
-}
-
 }  // namespace
 }  // namespace mxfa
 
@@ -985,51 +958,6 @@ int mxfa_seqlens_add_launch(void* seqlens, int is_int64, int B, int delta, void*
   return check_launch("seqlens_add_kernel");
 }
 
-// Work counter of the persistent prefill kernel, one per (context, stream):
-// launches on one stream run in order, so they can share it (each launch
-// leaves it zero).  Allocated on a stream's first launch outside graph
-// capture; a launch that finds none (first launch on a stream while it is
-// being captured, no context id, or too many streams) runs the fixed per-CTA
-// shares.  Keyed by the context's id, so a device whose context was torn
-// down and re-created gets a new counter instead of a freed one.
-static unsigned* prefill_sched_counter(cudaStream_t st) {
-  struct Key {
-    unsigned long long ctx;
-    uintptr_t stream;
-    bool operator==(const Key& o) const { return ctx == o.ctx && stream == o.stream; }
-  };
-  struct KeyHash {
-    size_t operator()(const Key& k) const { return std::hash<unsigned long long>()(k.ctx * 0x9E3779B97F4A7C15ull ^ k.stream); }
-  };
-  static std::mutex mu;
-  static std::unordered_map<Key, unsigned*, KeyHash> counters;
-  unsigned long long ctx = current_context_id();
-  if (ctx == 0) {  // no context current yet (a first call from a bare host): create the device's primary one
-    cudaFree(nullptr);
-    ctx = current_context_id();
-    if (ctx == 0) return nullptr;
-  }
-  const Key key{ctx, reinterpret_cast<uintptr_t>(st)};
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = counters.find(key);
-  if (it != counters.end()) return it->second;
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
-  if (counters.size() >= 4096) return nullptr;
-  void* ptr = nullptr;
-  if (cudaMalloc(&ptr, 2 * sizeof(unsigned)) != cudaSuccess) {
-    cudaGetLastError();
-    return nullptr;
-  }
-  if (cudaMemset(ptr, 0, 2 * sizeof(unsigned)) != cudaSuccess) {
-    cudaFree(ptr);
-    cudaGetLastError();
-    return nullptr;
-  }
-  counters.emplace(key, static_cast<unsigned*>(ptr));
-  return static_cast<unsigned*>(ptr);
-}
-
 static int varlen_fwd_impl(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
                            void* out, float* lse, int B, int max_q, int max_k, int total_q, int total_k, int HQ,
                            int HKV, int D, int causal, int bf16, float scale, void* stream, bool exact) {
@@ -1043,9 +971,7 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
     return fail(MXFA_ERR_INVALID, "dense layout needs total_q = B*max_q and total_k = B*max_k");
   if (!q || !k || !v || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
-  // work items are numbered (query tile * B + sequence) * HQ + head
-  if (static_cast<long long>((max_q + kTcRows - 1) / kTcRows) * B * HQ > INT_MAX)
-    return fail(MXFA_ERR_UNSUPPORTED, "too many query tiles");
+  if (HQ > 65535 || B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "grid too large");
   PrefillParams p{};
   p.q = q;
   p.k = k;
@@ -1063,7 +989,6 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  p.sched = prefill_sched_counter(st);
   // TMA maps cover exactly the token rows of q and k/v: boxes reaching past
   // the last row read zeros instead of memory beyond the tensors
   int dev = 0;
@@ -1081,9 +1006,7 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   const CUtensorMap& mq = maps.q;
   const CUtensorMap& mk = maps.k;
   const CUtensorMap& mv = maps.v;
-  // persistent: one CTA per SM (fewer when there are fewer query tiles)
-  const long long tiles = static_cast<long long>((max_q + kTcRows - 1) / kTcRows) * B * HQ;
-  dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
+  dim3 grid(HQ, B, (max_q + kTcRows - 1) / kTcRows);
   auto go = [&](auto kern, int smem, std::atomic<unsigned long long>& done, int threads) -> int {
     if (int rc = ensure_smem(kern, smem, done)) return rc;
     kern<<<grid, threads, smem, st>>>(p, mq, mk, mv);
@@ -1144,6 +1067,33 @@ namespace mxfa {
 namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[MXFA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+// Process-unique id of the calling thread's current context (0 if none or
+// the driver cannot say).  Context ids are never reused within a process,
+// unlike context handles.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 int noalloc_scratch(float** out) {
   static float* addr[64] = {};

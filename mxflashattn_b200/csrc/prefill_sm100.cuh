@@ -1,17 +1,14 @@
 // prefill_sm100.cuh -- attention forward on the 5th-generation tensor cores
 // (tcgen05 MMA, accumulators in tensor memory, operands staged by TMA).
 //
-// Persistent: one CTA per SM takes 128-row query tiles (one head each) from
-// a heaviest-first work list, one after another; 12 warps, specialised:
-//   warp 0    : TMA producer -- each tile's Q, then K and V tiles (128 keys)
-//               into three-stage rings, in the order the tensor pipe consumes
-//               them, running on into the next query tile; it also walks the
-//               work list and publishes the tiles to the other warps
+// CTA = one 128-row query tile of one head; 12 warps, specialised:
+//   warp 0    : TMA producer -- Q once, then K and V tiles (128 keys) into
+//               three-stage rings, in the order the tensor pipe consumes them
 //   warp 1    : allocates tensor memory; issues the P.V products
 //               O += P_j V_j (M=128, N=D, K=128; P from tensor memory, V MN-major)
 //   warp 2    : issues the score products S_j = Q K_j^T (M=128, N=128, K=D)
-//   warps 4-7 : softmax group 0 -- even key tiles of the CTA's tile stream
-//   warps 8-11: softmax group 1 -- odd key tiles
+//   warps 4-7 : softmax group 0 -- key tiles 0, 2, 4, ...
+//   warps 8-11: softmax group 1 -- key tiles 1, 3, 5, ...
 // Tensor memory: S/P buffers 0 | 1 | 2 (128 columns each) | O (D columns).
 // Tile j uses buffer j % 3, so the score products of the next two tiles are
 // ready while a group turns S_j into P_j (written over the columns of S_j it
@@ -42,10 +39,6 @@ struct PrefillParams {
   int B, Sq, Sk, HQ, HKV, GQ;
   int causal;
   float scale_log2;
-  // Optional work counter (two words, zero on entry, left zero): CTAs take
-  // list positions from it one at a time, so faster SMs take more tiles.
-  // Without it each CTA walks a fixed share of the list.
-  unsigned* sched;
 };
 
 // ------------------------------------------------------------ tcgen05 helpers
@@ -373,12 +366,11 @@ struct TcCfg {
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kTile;
   static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kMl = kQ;                       // epilogue (m, l) exchange over Q once every product is done
   static constexpr int kMPub = kV + kStages * kTile;   // [2 parities][128 rows] running max handed between groups
   static constexpr int kBar = kMPub + 2 * kTcRows * 4;
-  static constexpr int kRing = 8;                      // work items published ahead to the other roles
-  static constexpr int kNumBars = 1 + 2 * kStages + 3 * 3 + 2 * 4 + 1 + 2 * kRing;
-  // barriers, then the tensor-memory address, the abort flag, 8 spare bytes and the item ring
-  static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + kRing * 4 + 1024;
+  static constexpr int kNumBars = 1 + 2 * kStages + 3 * 3 + 2 * 4 + 1;
+  static constexpr int kSmemBytes = kBar + kNumBars * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = 512;           // S/P 0 | S/P 1 | S/P 2 | O
   static constexpr uint32_t kTmemO = 3 * kTcKeys;
   static constexpr int kSBufs = 3;
@@ -387,17 +379,15 @@ struct TcCfg {
 // K stage t%3 is released by S_t's completion (s_full) and V stage t%3 by
 // P.V_t's (pv_done): one commit per product, each barrier read by every
 // party that needs that product done.
-template <int kStages, int kRing>
+template <int kStages>
 struct TcBars {
   uint64_t q_full, k_full[kStages], v_full[kStages];
   uint64_t s_full[3], p_full[3], pv_done[3];
   uint64_t m_ready[2][4];  // [tile parity][warp quadrant]
-  // Completes once per work item, after its last P.V (and so every product of
-  // it): the epilogue must not wait on a per-buffer barrier by parity, since
-  // a group that ran out of tiles early can reach it two phases ahead of
-  // that barrier.
+  // Completes once, after the last P.V (and so every product): the epilogue
+  // must not wait on a per-buffer barrier by parity, since a group that ran
+  // out of tiles early can reach it two phases ahead of that barrier.
   uint64_t all_done;
-  uint64_t item_full[kRing], item_empty[kRing];  // the work-item ring
 };
 
 // One output accumulator, three score buffers.  A layout with an O per
@@ -440,130 +430,6 @@ struct TcBars {
 // (per 16-key chunk: 8 columns of P_hi, then 8 of P_lo) and both multiplied
 // with V, so P.V loses no precision to rounding P.  1.5x the tensor work;
 // for inputs whose V has a wide dynamic range.
-// bar.red.or over `threads` threads of barrier `id`: true when any thread's
-// predicate is true, the same answer in every thread.
-__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool pred) {
-  int r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %3, 0;\n\tbar.red.or.pred q, %1, %2, p;\n\t"
-      "selp.b32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(id), "r"(threads), "r"(pred ? 1 : 0)
-      : "memory");
-  return r != 0;
-}
-
-// Query tile work items, heaviest first: slice z (query tile qt = nqt-1-z,
-// the tile farthest into its sequence first) holds the (sequence, head)
-// pairs whose sequence has a query tile qt; within a slice sequences go in
-// index order and heads fastest.  Only tiles with rows exist in this list.
-// A work item is published to the other roles as code = (qt*B + b)*HQ + h.
-struct TcItem {
-  int h, b, q0, q_start, q_len, k_start, k_len, nkt;
-};
-
-__device__ __forceinline__ TcItem tc_item(const PrefillParams& p, int code) {
-  TcItem it;
-  it.h = code % p.HQ;
-  const int rest = code / p.HQ;
-  it.b = rest % p.B;
-  it.q0 = (rest / p.B) * kTcRows;
-  if (p.cu_q != nullptr) {
-    it.q_start = p.cu_q[it.b];
-    it.q_len = p.cu_q[it.b + 1] - it.q_start;
-    it.k_start = p.cu_k[it.b];
-    it.k_len = p.cu_k[it.b + 1] - it.k_start;
-  } else {
-    it.q_start = it.b * p.Sq;
-    it.q_len = p.Sq;
-    it.k_start = it.b * p.Sk;
-    it.k_len = p.Sk;
-  }
-  const int shift = it.k_len - it.q_len;
-  const int last_row = min(it.q0 + kTcRows, it.q_len) - 1;
-  const int k_end = p.causal ? min(it.k_len, last_row + shift + 1) : it.k_len;
-  it.nkt = k_end > 0 ? (k_end + kTcKeys - 1) / kTcKeys : 0;
-  return it;
-}
-
-// A CTA's walk over the work list (warp-collective: every lane holds the
-// same state).  With the shared counter each CTA takes the next free list
-// position whenever it needs an item; without it CTA c takes positions c,
-// 2G-1-c, 2G+c, 4G-1-c, ... (G CTAs), a snake that gives every CTA about the
-// same total of a heaviest-first list.  Either way a CTA's positions only
-// grow, and positions map to items through per-slice counts, so the walk
-// is incremental.
-struct TcWalk {
-  int r = 0;           // this CTA's items taken so far
-  int z = -1;          // current slice
-  long long cum = 0;   // list positions before slice z
-  int cnt = 0;         // sequences in slice z
-  bool done = false;
-
-  __device__ __forceinline__ int slice_seqs(const PrefillParams& p, int zz, int nqt, int lane) const {
-    const int thr = (nqt - 1 - zz) * kTcRows;
-    int c = 0;
-    for (int b0 = 0; b0 < p.B; b0 += 32) {
-      const int bb = b0 + lane;
-      const bool has = bb < p.B && (p.cu_q != nullptr ? p.cu_q[bb + 1] - p.cu_q[bb] : p.Sq) > thr;
-      c += __popc(__ballot_sync(0xffffffffu, has));
-    }
-    return c;
-  }
-  // next item code of this CTA, or -1 when the list is exhausted: from the
-  // shared counter when there is one, else the CTA's fixed share
-  __device__ __forceinline__ int next(const PrefillParams& p, int nqt, int lane) {
-    if (done) return -1;
-    long long k;
-    if (p.sched != nullptr) {
-      unsigned got = 0;
-      if (lane == 0) got = atomicAdd(p.sched, 1u);
-      k = __shfl_sync(0xffffffffu, got, 0);
-    } else {
-      const long long G = gridDim.x, c = blockIdx.x;
-      k = r * G + ((r & 1) ? G - 1 - c : c);
-    }
-    ++r;
-    while (k >= cum + static_cast<long long>(p.HQ) * cnt) {
-      cum += static_cast<long long>(p.HQ) * cnt;
-      if (++z >= nqt) {
-        done = true;
-        return -1;
-      }
-      cnt = slice_seqs(p, z, nqt, lane);
-    }
-    const int rin = static_cast<int>(k - cum);
-    int bi = rin / p.HQ;
-    const int thr = (nqt - 1 - z) * kTcRows;
-    int b = -1;
-    for (int b0 = 0; b0 < p.B && b < 0; b0 += 32) {
-      const int bb = b0 + lane;
-      const bool has = bb < p.B && (p.cu_q != nullptr ? p.cu_q[bb + 1] - p.cu_q[bb] : p.Sq) > thr;
-      unsigned m = __ballot_sync(0xffffffffu, has);
-      const int n = __popc(m);
-      if (bi < n) {
-        for (int i = 0; i < bi; ++i) m &= m - 1;
-        b = b0 + __ffs(m) - 1;
-      } else {
-        bi -= n;
-      }
-    }
-    if (b < 0) {  // unreachable when the counts above hold
-      done = true;
-      return -1;
-    }
-    return ((nqt - 1 - z) * p.B + b) * p.HQ + rin % p.HQ;
-  }
-};
-
-// Persistent: one CTA per SM takes query tiles (items) from the work list,
-// from the shared work counter when the launch has one, else its fixed
-// share.  The roles keep their own positions in one stream of key tiles
-// across items (tile t
-// uses K/V stage t%3 and S/P buffer t%3, barrier phases follow t), so the
-// next item's Q and first K tiles load, and its first score products run,
-// while this item's last tiles and epilogue finish.  The producer publishes
-// each item to the other roles through a shared-memory ring.
 template <typename T, int HD, bool kExactP = false>
 __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
@@ -572,19 +438,56 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
   constexpr int NS = Cfg::kStages;
   constexpr int NB = Cfg::kSBufs;
   constexpr int NG = Cfg::kGroups;
-  constexpr int NR = Cfg::kRing;
-  static_assert(NG == 2, "the epilogue exchange through the running-max slots assumes two groups");
+  static_assert(2 * NG * kTcRows * 4 <= Cfg::kTile, "epilogue exchange fits the Q tile");
   static_assert(Cfg::kTmemO + HD <= Cfg::kTmemCols, "tensor memory layout");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  TcBars<NS, NR>* bars = reinterpret_cast<TcBars<NS, NR>*>(sm + Cfg::kBar);
-  float* mpub = reinterpret_cast<float*>(sm + Cfg::kMPub);  // [tile parity][row]; epilogue exchange
+  TcBars<NS>* bars = reinterpret_cast<TcBars<NS>*>(sm + Cfg::kBar);
+  float* ml = reinterpret_cast<float*>(sm + Cfg::kMl);      // [group][m | l][row]
+  float* mpub = reinterpret_cast<float*>(sm + Cfg::kMPub);  // [tile parity][row]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kBar + Cfg::kNumBars * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
-  const int nqt = (p.Sq + kTcRows - 1) / kTcRows;
+
+  // Grid: x = query head, y = sequence, z = query tile (slowest).  Blocks go
+  // out in linear order, so every head and sequence's latest (heaviest, for
+  // causal) tiles start before any lighter tile: heaviest first across the
+  // whole grid, which leaves only light tiles for the tail.
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
+  const int hk = h / p.GQ;
+  int q_start, q_len, k_start, k_len;
+  if (p.cu_q != nullptr) {
+    q_start = p.cu_q[b];
+    q_len = p.cu_q[b + 1] - q_start;
+    k_start = p.cu_k[b];
+    k_len = p.cu_k[b + 1] - k_start;
+  } else {
+    q_start = b * p.Sq;
+    q_len = p.Sq;
+    k_start = b * p.Sk;
+    k_len = p.Sk;
+  }
+  const int qt = gridDim.z - 1 - blockIdx.z;
+  const int q0 = qt * kTcRows;
+  if (q0 >= q_len) return;
+  const int shift = k_len - q_len;
+  const int last_row = min(q0 + kTcRows, q_len) - 1;
+  const int k_end = p.causal ? min(k_len, last_row + shift + 1) : k_len;
+  const int nkt = k_end > 0 ? (k_end + kTcKeys - 1) / kTcKeys : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
   T* outp = static_cast<T*>(p.out);
+  if (nkt == 0) {  // every row of this tile sees no key: output 0, LSE -inf
+    if (warp >= 4 && warp < 8) {
+      const int r = (warp - 4) * 32 + lane;
+      if (q0 + r < q_len) {
+        T* orow = outp + (static_cast<size_t>(q_start + q0 + r) * p.HQ + h) * HD;
+        for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+        if (p.lse != nullptr) p.lse[static_cast<size_t>(q_start + q0 + r) * p.HQ + h] = -INFINITY;
+      }
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -600,10 +503,6 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
     for (int i = 0; i < 2; ++i)
       for (int qd = 0; qd < 4; ++qd) mbar_init(&bars->m_ready[i][qd], 32);
     mbar_init(&bars->all_done, 1);
-    for (int i = 0; i < NR; ++i) {
-      mbar_init(&bars->item_full[i], 1);
-      mbar_init(&bars->item_empty[i], 3 + NG * kTcGroupWarps);  // producer, both issuers, every softmax warp
-    }
     *abort = 0;
     fence_mbar_init();
   }
@@ -616,139 +515,42 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // the consumers' read of item n from the ring (false: end of the list or abort)
-  auto take_item = [&](int n, int& code) -> bool {
-    if (!tc_wait(&bars->item_full[n % NR], (n / NR) & 1, abort)) return false;
-    code = ring[n % NR];
-    return code >= 0;
-  };
-
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // The K cursor walks the list up to three tiles ahead and publishes each
-    // item with key tiles (a tile whose rows see no key is written as zeros
-    // here and never published); the V cursor follows the published items at
-    // the tile being released for V, loads each next item's Q once the score
-    // products of the item before have read the current one, and releases
-    // an item's ring slot (with every other role) when it is past it.
-    TcWalk kwalk;
-    int n_pub = 0;
-    auto publish = [&](int code) -> bool {
-      const int slot = n_pub % NR;
-      if (n_pub >= NR && !tc_wait(&bars->item_empty[slot], ((n_pub / NR) - 1) & 1, abort)) return false;
-      if (lane == 0) {
-        ring[slot] = code;
-        mbar_arrive(&bars->item_full[slot]);
-      }
-      __syncwarp();
-      ++n_pub;
-      return true;
-    };
-    // K cursor: its item and the tile within it
-    TcItem kit{};
-    int kj = 0, kcode = -1;
-    bool k_end = false;
-    auto k_next_item = [&]() {
-      for (;;) {
-        kcode = kwalk.next(p, nqt, lane);
-        if (kcode < 0) {
-          publish(-1);
-          k_end = true;
-          return;
-        }
-        kit = tc_item(p, kcode);
-        if (kit.nkt > 0) break;
-        // no row of this tile sees a key: output 0, LSE -inf, written here
-        for (int rr = lane; rr < kTcRows; rr += 32) {
-          const int qi = kit.q0 + rr;
-          if (qi >= kit.q_len) break;
-          T* orow = outp + (static_cast<size_t>(kit.q_start + qi) * p.HQ + kit.h) * HD;
-          for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-          if (p.lse != nullptr) p.lse[static_cast<size_t>(kit.q_start + qi) * p.HQ + kit.h] = -INFINITY;
-        }
-      }
-      publish(kcode);
-      kj = 0;
-    };
-    auto load_k = [&](int t) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->k_full[t % NS], Cfg::kTile);
-#pragma unroll
-        for (int db = 0; db < Cfg::kDBlk; ++db)
-          tma_load_3d(sm + Cfg::kK + (t % NS) * Cfg::kTile + db * Cfg::kBlk, &tmk, &bars->k_full[t % NS], db * 64,
-                      kit.h / p.GQ, kit.k_start + kj * kTcKeys);
-      }
-      __syncwarp();
-    };
-    auto load_q = [&](const TcItem& it) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->q_full, Cfg::kTile);
-#pragma unroll
-        for (int db = 0; db < Cfg::kDBlk; ++db)
-          tma_load_3d(sm + Cfg::kQ + db * Cfg::kBlk, &tmq, &bars->q_full, db * 64, it.h, it.q_start + it.q0);
-      }
-      __syncwarp();
-    };
     if (lane == 0) {
       prefetch_tensormap(&tmq);
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
-    }
-    k_next_item();
-    int kt = 0;  // global index of the next K tile to load
-    for (; kt < NS && !k_end; ++kt) {
-      load_k(kt);
-      if (++kj == kit.nkt) k_next_item();
-    }
-    // the V cursor's items come from the ring: published by the K cursor of
-    // this warp before the V cursor needs them (it is at least one tile ahead)
-    int nv = 0;
-    auto v_item = [&](int n, TcItem& it) -> bool {
-      const int code = ring[n % NR];
-      if (code < 0) return false;
-      it = tc_item(p, code);
-      return true;
-    };
-    TcItem vit{};
-    bool v_has = v_item(0, vit);
-    if (v_has) load_q(vit);
-    int vj = 0;
-    for (int t = 0; v_has && !*abort; ++t) {
-      const int st = t % NS, use = t / NS;
-      if (use > 0 && !tc_wait(&bars->pv_done[st], (use - 1) & 1, abort)) break;  // P.V_{t-3} done
-      if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->q_full, Cfg::kTile);
+#pragma unroll
+      for (int db = 0; db < Cfg::kDBlk; ++db)
+        tma_load_3d(sm + Cfg::kQ + db * Cfg::kBlk, &tmq, &bars->q_full, db * 64, h, q_start + q0);
+      // Issue order = consumption order: K_0..K_2, then per tile V_t and K_{t+3}.
+      // K_{t+3} replaces K_t once S_t is done; V_t replaces V_{t-3} once P.V_{t-3}
+      // is done.  Neither copy ever waits behind a wait of the other kind that
+      // the tensor pipe reaches later.
+      auto load_k = [&](int t) {
+        mbar_arrive_expect_tx(&bars->k_full[t % NS], Cfg::kTile);
+#pragma unroll
+        for (int db = 0; db < Cfg::kDBlk; ++db)
+          tma_load_3d(sm + Cfg::kK + (t % NS) * Cfg::kTile + db * Cfg::kBlk, &tmk, &bars->k_full[t % NS], db * 64,
+                      hk, k_start + t * kTcKeys);
+      };
+      for (int t = 0; t < NS && t < nkt; ++t) load_k(t);
+      for (int t = 0; t < nkt && !*abort; ++t) {
+        const int st = t % NS, use = t / NS;
+        if (use > 0 && !tc_wait(&bars->pv_done[st], (use - 1) & 1, abort)) break;  // P.V_{t-3} done
         mbar_arrive_expect_tx(&bars->v_full[st], Cfg::kTile);
 #pragma unroll
         for (int db = 0; db < Cfg::kDBlk; ++db)
-          tma_load_3d(sm + Cfg::kV + st * Cfg::kTile + db * Cfg::kBlk, &tmv, &bars->v_full[st], db * 64,
-                      vit.h / p.GQ, vit.k_start + vj * kTcKeys);
-      }
-      __syncwarp();
-      const bool item_last = vj + 1 == vit.nkt;
-      // the next item starts at tile t+1, whose K is loaded: it is published (or the end is)
-      TcItem vnext{};
-      const bool v_has_next = item_last && v_item(nv + 1, vnext);
-      if ((kt == t + NS && !k_end) || v_has_next) {
-        if (!tc_wait(&bars->s_full[st], use & 1, abort)) break;  // S_t done with K stage t%3 (and with Q)
-        if (v_has_next) load_q(vnext);
-        if (kt == t + NS && !k_end) {
-          load_k(kt);
-          ++kt;
-          if (++kj == kit.nkt) k_next_item();
+          tma_load_3d(sm + Cfg::kV + st * Cfg::kTile + db * Cfg::kBlk, &tmv, &bars->v_full[st], db * 64, hk,
+                      k_start + t * kTcKeys);
+        if (t + NS < nkt) {
+          if (!tc_wait(&bars->s_full[st], use & 1, abort)) break;  // S_t done with this stage
+          load_k(t + NS);
         }
       }
-      if (item_last) {
-        if (lane == 0) mbar_arrive(&bars->item_empty[nv % NR]);
-        ++nv;
-        vit = vnext;
-        v_has = v_has_next;
-        vj = 0;
-      } else {
-        ++vj;
-      }
     }
-    // items left unpublished when a wait gave up: let the consumers stop
-    while (!k_end && *abort == 0) k_next_item();
   } else if (warp == 1 || warp == 2) {
     // ------------------------------------------------------------ MMA issue
     // Two issuing threads: warp 1 issues the P.V products, warp 2 the score
@@ -763,357 +565,313 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
       constexpr uint32_t idesc_o = umma_idesc<T>(kTcRows, HD, true);
       constexpr int kS = HD / 16;        // K-steps of a score product
       constexpr int kP = kTcKeys / 16;   // K-steps of a P.V product
-      int t = 0, ni = 0;
-      for (int n = 0;; ++n) {
-        int code;
-        const bool more = take_item(n, code);
-        mbar_arrive(&bars->item_empty[n % NR]);
-        if (!more) break;
-        const int nkt = tc_item(p, code).nkt;  // >= 1: items without key tiles are never published
-        bool ok = true;
-        if (warp == 2) {
-          auto s_step = [](int kk) -> uint64_t { return (kk >> 2) * (Cfg::kBlk >> 4) + (kk & 3) * 2; };
-          uint64_t qd[kS];
-          {
-            const uint64_t base = smem_desc(smem_u32(sm + Cfg::kQ), 16, 1024);
+      if (warp == 2) {
+        auto s_step = [](int kk) -> uint64_t { return (kk >> 2) * (Cfg::kBlk >> 4) + (kk & 3) * 2; };
+        uint64_t qd[kS];
+        {
+          const uint64_t base = smem_desc(smem_u32(sm + Cfg::kQ), 16, 1024);
 #pragma unroll
-            for (int kk = 0; kk < kS; ++kk) qd[kk] = base + s_step(kk);
-          }
-          ok = tc_wait(&bars->q_full, ni & 1, abort);
-          for (int j = 0; j < nkt && ok; ++j, ++t) {
-            const int buf = t % NB, ks = t % NS;
-            uint64_t kd[kS];
-            {
-              const uint64_t base = smem_desc(smem_u32(sm + Cfg::kK + ks * Cfg::kTile), 16, 1024);
-#pragma unroll
-              for (int kk = 0; kk < kS; ++kk) kd[kk] = base + s_step(kk);
-            }
-            pin_regs(kd);
-            if (t >= NB && !tc_wait(&bars->pv_done[buf], ((t - NB) / NB) & 1, abort)) ok = false;  // buffer free
-            if (ok && !tc_wait(&bars->k_full[ks], (t / NS) & 1, abort)) ok = false;
-            if (!ok) break;
-            tc_fence_after();
-            umma_ss_chain(tmem + buf * kTcKeys, qd, kd, idesc_s);
-            umma_commit(&bars->s_full[buf]);
-          }
-        } else {
-          for (int j = 0; j < nkt; ++j, ++t) {
-            const int buf = t % NB, vs = t % NS;
-            uint64_t vd[kP];
-            uint32_t pa[kP], pl[kP];
-            {
-              const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
-#pragma unroll
-              for (int kk = 0; kk < kP; ++kk) {
-                vd[kk] = vbase + kk * (16 * 128 >> 4);
-                // P_t packed over the columns of S_t: 8 columns per 16 keys, or
-                // (exact P) P_hi then P_lo in the 16 columns of each 16 keys
-                pa[kk] = tmem + buf * kTcKeys + (kExactP ? kk * 16 : kk * 8);
-                pl[kk] = pa[kk] + 8;
-              }
-            }
-            pin_regs(vd);
-            pin_regs(pa);
-            if (!tc_wait(&bars->v_full[vs], (t / NS) & 1, abort)) ok = false;
-            if (ok && !tc_wait(&bars->p_full[buf], (t / NB) & 1, abort)) ok = false;
-            if (!ok) break;
-            tc_fence_after();
-            // the item's first product starts O afresh: the epilogue of the
-            // item before read O before any softmax warp released P_t
-            umma_ts_chain(tmem + Cfg::kTmemO, pa, vd, idesc_o, j > 0 ? 1u : 0u);
-            if constexpr (kExactP) umma_ts_chain(tmem + Cfg::kTmemO, pl, vd, idesc_o, 1u);
-            umma_commit(&bars->pv_done[buf]);
-            // every score product of the item completed before its last P
-            // existed, so this marks the end of the item's products
-            if (j == nkt - 1) umma_commit(&bars->all_done);
-          }
+          for (int kk = 0; kk < kS; ++kk) qd[kk] = base + s_step(kk);
         }
-        if (!ok) break;
-        ++ni;
+        bool ok = tc_wait(&bars->q_full, 0, abort);
+        for (int t = 0; t < nkt && ok; ++t) {
+          const int buf = t % NB, ks = t % NS;
+          uint64_t kd[kS];
+          {
+            const uint64_t base = smem_desc(smem_u32(sm + Cfg::kK + ks * Cfg::kTile), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kS; ++kk) kd[kk] = base + s_step(kk);
+          }
+          pin_regs(kd);
+          if (t >= NB && !tc_wait(&bars->pv_done[buf], ((t - NB) / NB) & 1, abort)) break;  // buffer free
+          if (!tc_wait(&bars->k_full[ks], (t / NS) & 1, abort)) break;
+          tc_fence_after();
+          umma_ss_chain(tmem + buf * kTcKeys, qd, kd, idesc_s);
+          umma_commit(&bars->s_full[buf]);
+        }
+      } else {
+        for (int j = 0; j < nkt; ++j) {
+          const int buf = j % NB, vs = j % NS;
+          uint64_t vd[kP];
+          uint32_t pa[kP], pl[kP];
+          {
+            const uint64_t vbase = smem_desc(smem_u32(sm + Cfg::kV + vs * Cfg::kTile), Cfg::kBlk, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kP; ++kk) {
+              vd[kk] = vbase + kk * (16 * 128 >> 4);
+              // P_j packed over the columns of S_j: 8 columns per 16 keys, or
+              // (exact P) P_hi then P_lo in the 16 columns of each 16 keys
+              pa[kk] = tmem + buf * kTcKeys + (kExactP ? kk * 16 : kk * 8);
+              pl[kk] = pa[kk] + 8;
+            }
+          }
+          pin_regs(vd);
+          pin_regs(pa);
+          if (!tc_wait(&bars->v_full[vs], (j / NS) & 1, abort)) break;
+          if (!tc_wait(&bars->p_full[buf], (j / NB) & 1, abort)) break;
+          tc_fence_after();
+          umma_ts_chain(tmem + Cfg::kTmemO, pa, vd, idesc_o, j > 0 ? 1u : 0u);
+          if constexpr (kExactP) umma_ts_chain(tmem + Cfg::kTmemO, pl, vd, idesc_o, 1u);
+          umma_commit(&bars->pv_done[buf]);
+          // every score product completed before P_{nkt-1} existed, so this
+          // marks the end of all tensor-memory and shared-memory reads
+          if (j == nkt - 1) umma_commit(&bars->all_done);
+        }
       }
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
-    const int g = (warp - 4) >> 2;          // group: global key tiles t with t % NG == g
+    const int g = (warp - 4) >> 2;          // group: key tiles j with j % NG == g
     const int quad = warp & 3;              // tensor-memory lane quadrant
     const int r = quad * 32 + lane;         // query row within the tile == tensor-memory lane
+    const int qi = q0 + r;                  // query index within the sequence
     const uint32_t lane_base = tmem + ((static_cast<uint32_t>(quad) * 32u) << 16);
     const uint32_t o_base = lane_base + Cfg::kTmemO;
+    const int vis_end = p.causal ? min(k_len, qi + shift + 1) : k_len;  // keys [0, vis_end) visible
     const float sc = p.scale_log2;
+    float m_own = -INFINITY, l_own = 0.f;   // this group's row sum, at the maximum of its last tile
     bool ok = true;
-    int t = 0, ni = 0;
-    for (int n = 0;; ++n) {
-      int code;
-      const bool more = __all_sync(0xffffffffu, take_item(n, code));
-      if (lane == 0) mbar_arrive(&bars->item_empty[n % NR]);
-      // every softmax warp takes the same decision (they meet at barriers below)
-      if (named_barrier_or(1, NG * kTcGroupWarps * 32, !more)) break;
-      int nkt, vis_end;  // only these stay live through the tiles; the epilogue decodes the item again
-      {
-        const TcItem it = tc_item(p, code);
-        nkt = it.nkt;
-        vis_end = p.causal ? min(it.k_len, it.q0 + r + it.k_len - it.q_len + 1) : it.k_len;  // keys [0, vis_end) visible
+    for (int j = g; j < nkt; j += NG) {
+      const int buf = j % NB;
+      if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[buf], (j / NB) & 1, abort))) {
+        ok = false;
+        break;
       }
-      float m_own = -INFINITY, l_own = 0.f;   // this group's row sum, at the maximum of its last tile
-      for (int j = ((t & 1) == g) ? 0 : 1; j < nkt; j += NG) {
-        const int Tg = t + j;
-        const int buf = Tg % NB;
-        if (!__all_sync(0xffffffffu, tc_wait(&bars->s_full[buf], (Tg / NB) & 1, abort))) {
+      tc_fence_after();
+      const uint32_t sbuf = lane_base + buf * kTcKeys;
+      const int key0 = j * kTcKeys;
+      const bool full = key0 + kTcKeys <= vis_end;
+
+      // pass 1: the row's extreme raw score over visible keys (max for a
+      // positive scale, min for a negative one), scaled into the log2 domain
+      const bool all_full = __all_sync(0xffffffffu, full);
+      const bool pos = sc >= 0.f;
+      const float ext0 = pos ? -INFINITY : INFINITY;
+      float ext = ext0;
+      uint32_t ra[32], rb[32];
+      if (all_full) {
+        // 32-column loads, each in flight while the previous chunk is
+        // compared (four chains).  The last chunk stays in registers for
+        // pass 2, whose first load goes out before the maximum exchange.
+        float e[4] = {ext0, ext0, ext0, ext0};
+        tmem_ld32_async(sbuf, ra);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 32, rb);
+        ext_chunk32(ra, pos, e);
+        tmem_wait_ld(rb);
+        tmem_ld32_async(sbuf + 64, ra);
+        ext_chunk32(rb, pos, e);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 96, rb);
+        ext_chunk32(ra, pos, e);
+        tmem_wait_ld(rb);
+        if constexpr (!kExactP) tmem_ld32_async(sbuf, ra);
+        ext_chunk32(rb, pos, e);
+        ext = pos ? fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])) : fminf(fminf(e[0], e[1]), fminf(e[2], e[3]));
+      } else {
+        // diagonal tile: a rolled loop over 16-column chunks keeps this
+        // rarely taken path out of the way of the unrolled one
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float v = __uint_as_float(raw[i]);
+            const bool vis = key0 + c + i < vis_end;
+            ext = vis ? (pos ? fmaxf(ext, v) : fminf(ext, v)) : ext;
+          }
+        }
+      }
+      const float mx = (ext == INFINITY || ext == -INFINITY) ? -INFINITY : ext * sc;
+
+      // the running maximum after tile j-1, from the other group
+      float m_in = -INFINITY;
+      if (j > 0) {
+        const int pj = j - 1;
+        if (!__all_sync(0xffffffffu, tc_wait(&bars->m_ready[pj & 1][quad], (pj >> 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        m_in = mpub[(pj & 1) * kTcRows + r];
+      }
+      const float m_j = mx > m_in + kRescaleThreshold ? mx : m_in;
+      // every lane releases its own row's value (arrival count 32)
+      mpub[(j & 1) * kTcRows + r] = m_j;
+      mbar_arrive(&bars->m_ready[j & 1][quad]);
+
+      if (m_j != m_own) {  // this group's sum follows the maximum it now uses
+        l_own *= fast_exp2(m_own - m_j);  // 0 when m_own = -inf
+        m_own = m_j;
+      }
+      // O holds tiles < j at m_in; bring it to m_j once P.V_{j-1} is done
+      // (P.V_j cannot start before this group releases P_j)
+      const bool grow = j > 0 && m_j != m_in;
+      if (__any_sync(0xffffffffu, grow)) {
+        const int pj = j - 1;
+        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv_done[pj % NB], (pj / NB) & 1, abort))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sbuf = lane_base + buf * kTcKeys;
-        const int key0 = j * kTcKeys;
-        const bool full = key0 + kTcKeys <= vis_end;
-
-        // pass 1: the row's extreme raw score over visible keys (max for a
-        // positive scale, min for a negative one), scaled into the log2 domain
-        const bool all_full = __all_sync(0xffffffffu, full);
-        const bool pos = sc >= 0.f;
-        const float ext0 = pos ? -INFINITY : INFINITY;
-        float ext = ext0;
-        uint32_t ra[32], rb[32];
-        if (all_full) {
-          // 32-column loads, each in flight while the previous chunk is
-          // compared (four chains).  The last chunk stays in registers for
-          // pass 2, whose first load goes out before the maximum exchange.
-          float e[4] = {ext0, ext0, ext0, ext0};
-          tmem_ld32_async(sbuf, ra);
-          tmem_wait_ld(ra);
-          tmem_ld32_async(sbuf + 32, rb);
-          ext_chunk32(ra, pos, e);
-          tmem_wait_ld(rb);
-          tmem_ld32_async(sbuf + 64, ra);
-          ext_chunk32(rb, pos, e);
-          tmem_wait_ld(ra);
-          tmem_ld32_async(sbuf + 96, rb);
-          ext_chunk32(ra, pos, e);
-          tmem_wait_ld(rb);
-          if constexpr (!kExactP) tmem_ld32_async(sbuf, ra);
-          ext_chunk32(rb, pos, e);
-          ext = pos ? fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])) : fminf(fminf(e[0], e[1]), fminf(e[2], e[3]));
-        } else {
-          // diagonal tile: a rolled loop over 16-column chunks keeps this
-          // rarely taken path out of the way of the unrolled one
-#pragma unroll 1
-          for (int c = 0; c < kTcKeys; c += 16) {
-            uint32_t raw[16];
-            tmem_ld16(sbuf + c, raw);
+        const float alpha = grow ? fast_exp2(m_in - m_j) : 1.f;  // 0 when m_in = -inf
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float v = __uint_as_float(raw[i]);
-              const bool vis = key0 + c + i < vis_end;
-              ext = vis ? (pos ? fmaxf(ext, v) : fminf(ext, v)) : ext;
-            }
-          }
-        }
-        const float mx = (ext == INFINITY || ext == -INFINITY) ? -INFINITY : ext * sc;
-
-        // the running maximum after tile j-1, from the other group
-        float m_in = -INFINITY;
-        if (j > 0) {
-          const int pj = Tg - 1;
-          if (!__all_sync(0xffffffffu, tc_wait(&bars->m_ready[pj & 1][quad], (pj >> 1) & 1, abort))) {
-            ok = false;
-            break;
-          }
-          m_in = mpub[(pj & 1) * kTcRows + r];
-        }
-        const float m_j = mx > m_in + kRescaleThreshold ? mx : m_in;
-        // every lane releases its own row's value (arrival count 32)
-        mpub[(Tg & 1) * kTcRows + r] = m_j;
-        mbar_arrive(&bars->m_ready[Tg & 1][quad]);
-
-        if (m_j != m_own) {  // this group's sum follows the maximum it now uses
-          l_own *= fast_exp2(m_own - m_j);  // 0 when m_own = -inf
-          m_own = m_j;
-        }
-        // O holds tiles < j at m_in; bring it to m_j once P.V_{j-1} is done
-        // (P.V_j cannot start before this group releases P_j)
-        const bool grow = j > 0 && m_j != m_in;
-        if (__any_sync(0xffffffffu, grow)) {
-          const int pj = Tg - 1;
-          if (!__all_sync(0xffffffffu, tc_wait(&bars->pv_done[pj % NB], (pj / NB) & 1, abort))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float alpha = grow ? fast_exp2(m_in - m_j) : 1.f;  // 0 when m_in = -inf
-#pragma unroll
-          for (int c = 0; c < HD; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(o_base + c, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(o_base + c, o);
-          }
-        }
-
-        // pass 2: P = 2^(s*scale - m_j), packed in pairs into columns of S
-        // that were already read
-        float rs = 0.f;
-        const float neg_m = -m_j;
-        if (kExactP && all_full) {
-          // 64-key halves read at once; per 16-key chunk, P_hi then P_lo in the
-          // chunk's own (already read) columns, stored 32 columns at a time
-          float r0 = 0.f, r1 = 0.f;
-#pragma unroll 1
-          for (int c = 0; c < kTcKeys; c += 64) {
-            uint32_t raw[64];
-            tmem_ld64(sbuf + c, raw);
-#pragma unroll
-            for (int qq = 0; qq < 2; ++qq) {
-              uint32_t packed[32];
-#pragma unroll
-              for (int i = 0; i < 32; i += 2) {
-                const float p0 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i]), sc, neg_m));
-                const float p1 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i + 1]), sc, neg_m));
-                r0 += p0;
-                r1 += p1;
-                const uint32_t hi = Elem<T>::pack(p0, p1);
-                const float2 hf = Elem<T>::unpack(hi);
-                const int w = (i >> 4) * 16 + ((i & 15) >> 1);  // chunk i/16: hi words 0-7, lo words 8-15
-                packed[w] = hi;
-                packed[w + 8] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
-              }
-              tmem_st32(sbuf + c + 32 * qq, packed);
-            }
-          }
-          rs = r0 + r1;
-        } else if constexpr (kExactP) {
-          // diagonal tile, 16-key chunks: P_hi and P_lo land in the chunk's own (already read) columns
-          const bool live = m_j != -INFINITY;
-#pragma unroll 1
-          for (int c = 0; c < kTcKeys; c += 16) {
-            uint32_t raw[16];
-            tmem_ld16(sbuf + c, raw);
-            uint32_t packed[16];
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              const bool v0 = live && (all_full || key0 + c + i < vis_end);
-              const bool v1 = live && (all_full || key0 + c + i + 1 < vis_end);
-              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
-              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
-              rs += p0 + p1;
-              const uint32_t hi = Elem<T>::pack(p0, p1);
-              const float2 hf = Elem<T>::unpack(hi);
-              packed[i >> 1] = hi;
-              packed[8 + (i >> 1)] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
-            }
-            tmem_st16(sbuf + c, packed);
-          }
-        } else if (all_full) {  // every row sees every key of the tile, so m_j is finite
-          // rb holds columns 96-127 from pass 1 and ra's load of columns 0-31
-          // is in flight; each later load overlaps the previous chunk's exp2.
-          // P of columns [32k, 32k+32) goes to columns [16k, 16k+16), which
-          // lie in columns already read; the stores are waited on once.
-          const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
-          uint64_t acc0 = 0, acc1 = 0;  // four sum chains: columns i % 4
-          uint32_t pk3[16], pka[16], pkb[16];
-          exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pk3);
-          tmem_wait_ld(ra);
-          tmem_ld32_async(sbuf + 32, rb);
-          exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
-          tmem_st16_async(sbuf, pka);
-          tmem_wait_ld(rb);
-          tmem_ld32_async(sbuf + 64, ra);
-          exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pkb);
-          tmem_st16_async(sbuf + 16, pkb);
-          tmem_st16_async(sbuf + 48, pk3);  // columns 48-63 were read with chunk 1
-          tmem_wait_ld(ra);
-          tmem_wait_st();  // pka is written again below
-          exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
-          tmem_st16_async(sbuf + 32, pka);
-          tmem_wait_st();
-          float a, bb;
-          f2_unpack(f2_add(acc0, acc1), a, bb);
-          rs = a + bb;
-        } else {
-          const bool live = m_j != -INFINITY;
-#pragma unroll 1
-          for (int c = 0; c < kTcKeys; c += 16) {
-            uint32_t raw[16];
-            tmem_ld16(sbuf + c, raw);
-            uint32_t packed[8];
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              const bool v0 = live && key0 + c + i < vis_end;
-              const bool v1 = live && key0 + c + i + 1 < vis_end;
-              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
-              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
-              rs += p0 + p1;
-              packed[i >> 1] = Elem<T>::pack(p0, p1);
-            }
-            // P columns [c/2, c/2 + 8) lie in the S columns already read
-            tmem_st8(sbuf + (c >> 1), packed);
-          }
-        }
-        l_own += rs;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_full[buf]);
-      }
-      t += nkt;
-
-      // ------------------------------------------------------ merge + store
-      // Every product of the item is complete once its last P.V is (and every
-      // read of the running-max slots with it); the slots then carry the
-      // groups' (m, l) exchange.
-      const bool done_ok = __all_sync(0xffffffffu, ok && tc_wait(&bars->all_done, ni & 1, abort));
-      if (g == 1) {
-        mpub[r] = m_own;
-        mpub[kTcRows + r] = l_own;
-      }
-      named_barrier_sync(1, NG * kTcGroupWarps * 32);
-      float M = m_own, inv = 0.f, L = 0.f;
-      if (g == 0) {
-        const float m1 = mpub[r], l1 = mpub[kTcRows + r];
-        M = fmaxf(m_own, m1);  // the last tile's maximum, at which O is held
-        if (m_own != -INFINITY) L += l_own * fast_exp2(m_own - M);
-        if (m1 != -INFINITY) L += l1 * fast_exp2(m1 - M);
-        inv = L > 0.f ? 1.f / L : 0.f;
-        mpub[r] = M;
-        mpub[kTcRows + r] = inv;
-      }
-      named_barrier_sync(1, NG * kTcGroupWarps * 32);
-      if (g == 1) {
-        M = mpub[r];
-        inv = mpub[kTcRows + r];
-      }
-      if (done_ok) {
-        tc_fence_after();
-        const TcItem it = tc_item(p, code);
-        const int h = it.h, q_start = it.q_start, q_len = it.q_len, qi = it.q0 + r;
-        T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
-        // group g stores the 32-column chunks g, g + NG, ...
-        for (int c = g * 32; c < HD; c += NG * 32) {
+        for (int c = 0; c < HD; c += 32) {
           uint32_t o[32];
           tmem_ld32(o_base + c, o);
-          if (qi < q_len) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 v;
-              v.x = Elem<T>::pack(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
-              v.y = Elem<T>::pack(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-              v.z = Elem<T>::pack(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-              v.w = Elem<T>::pack(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + c + i) = v;
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_base + c, o);
+        }
+      }
+
+      // pass 2: P = 2^(s*scale - m_j), packed in pairs into columns of S
+      // that were already read
+      float rs = 0.f;
+      const float neg_m = -m_j;
+      if (kExactP && all_full) {
+        // 64-key halves read at once; per 16-key chunk, P_hi then P_lo in the
+        // chunk's own (already read) columns, stored 32 columns at a time
+        float r0 = 0.f, r1 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 64) {
+          uint32_t raw[64];
+          tmem_ld64(sbuf + c, raw);
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            uint32_t packed[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i]), sc, neg_m));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(raw[32 * qq + i + 1]), sc, neg_m));
+              r0 += p0;
+              r1 += p1;
+              const uint32_t hi = Elem<T>::pack(p0, p1);
+              const float2 hf = Elem<T>::unpack(hi);
+              const int w = (i >> 4) * 16 + ((i & 15) >> 1);  // chunk i/16: hi words 0-7, lo words 8-15
+              packed[w] = hi;
+              packed[w + 8] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
             }
+            tmem_st32(sbuf + c + 32 * qq, packed);
           }
         }
-        if (g == 0 && qi < q_len && p.lse != nullptr)
-          p.lse[static_cast<size_t>(q_start + qi) * p.HQ + h] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+        rs = r0 + r1;
+      } else if constexpr (kExactP) {
+        // diagonal tile, 16-key chunks: P_hi and P_lo land in the chunk's own (already read) columns
+        const bool live = m_j != -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const bool v0 = live && (all_full || key0 + c + i < vis_end);
+            const bool v1 = live && (all_full || key0 + c + i + 1 < vis_end);
+            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
+            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
+            rs += p0 + p1;
+            const uint32_t hi = Elem<T>::pack(p0, p1);
+            const float2 hf = Elem<T>::unpack(hi);
+            packed[i >> 1] = hi;
+            packed[8 + (i >> 1)] = Elem<T>::pack(p0 - hf.x, p1 - hf.y);
+          }
+          tmem_st16(sbuf + c, packed);
+        }
+      } else if (all_full) {  // every row sees every key of the tile, so m_j is finite
+        // rb holds columns 96-127 from pass 1 and ra's load of columns 0-31
+        // is in flight; each later load overlaps the previous chunk's exp2.
+        // P of columns [32k, 32k+32) goes to columns [16k, 16k+16), which
+        // lie in columns already read; the stores are waited on once.
+        const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc0 = 0, acc1 = 0;  // four sum chains: columns i % 4
+        uint32_t pk3[16], pka[16], pkb[16];
+        exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pk3);
+        tmem_wait_ld(ra);
+        tmem_ld32_async(sbuf + 32, rb);
+        exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
+        tmem_st16_async(sbuf, pka);
+        tmem_wait_ld(rb);
+        tmem_ld32_async(sbuf + 64, ra);
+        exp2_chunk32<T>(rb, sc2, nm2, acc0, acc1, pkb);
+        tmem_st16_async(sbuf + 16, pkb);
+        tmem_st16_async(sbuf + 48, pk3);  // columns 48-63 were read with chunk 1
+        tmem_wait_ld(ra);
+        tmem_wait_st();  // pka is written again below
+        exp2_chunk32<T>(ra, sc2, nm2, acc0, acc1, pka);
+        tmem_st16_async(sbuf + 32, pka);
+        tmem_wait_st();
+        float a, bb;
+        f2_unpack(f2_add(acc0, acc1), a, bb);
+        rs = a + bb;
+      } else {
+        const bool live = m_j != -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTcKeys; c += 16) {
+          uint32_t raw[16];
+          tmem_ld16(sbuf + c, raw);
+          uint32_t packed[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const bool v0 = live && key0 + c + i < vis_end;
+            const bool v1 = live && key0 + c + i + 1 < vis_end;
+            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(raw[i]), sc, neg_m)) : 0.f;
+            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(raw[i + 1]), sc, neg_m)) : 0.f;
+            rs += p0 + p1;
+            packed[i >> 1] = Elem<T>::pack(p0, p1);
+          }
+          // P columns [c/2, c/2 + 8) lie in the S columns already read
+          tmem_st8(sbuf + (c >> 1), packed);
+        }
       }
-      // O is read and the slots are free again before any P of the next item
-      // (and with it that item's first P.V product, which starts O afresh);
-      // a wait that gave up in any warp stops every softmax warp here
+      l_own += rs;
       tc_fence_before();
-      if (named_barrier_or(1, NG * kTcGroupWarps * 32, !(ok && done_ok))) break;
-      ++ni;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[buf]);
     }
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");  // a load left in flight by an aborted tile
+
+    // ---------------------------------------------------------- merge + store
+    // Every product is complete once the last P.V is; the Q tile's shared
+    // memory is then free for the (m, l) exchange.
+    const bool done_ok = __all_sync(0xffffffffu, ok && tc_wait(&bars->all_done, 0, abort));
+    fence_proxy_async_smem();
+    ml[(g * 2) * kTcRows + r] = m_own;
+    ml[(g * 2 + 1) * kTcRows + r] = l_own;
+    named_barrier_sync(1, NG * kTcGroupWarps * 32);
+    if (done_ok) {
+      tc_fence_after();
+      float M = -INFINITY;  // the last tile's maximum, at which O is held
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) M = fmaxf(M, ml[(gg * 2) * kTcRows + r]);
+      float L = 0.f;
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        const float mg = ml[(gg * 2) * kTcRows + r];
+        if (mg != -INFINITY) L += ml[(gg * 2 + 1) * kTcRows + r] * fast_exp2(mg - M);
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      T* orow = outp + (static_cast<size_t>(q_start + qi) * p.HQ + h) * HD;
+      // group g stores the 32-column chunks g, g + NG, ...
+      for (int c = g * 32; c < HD; c += NG * 32) {
+        uint32_t o[32];
+        tmem_ld32(o_base + c, o);
+        if (qi < q_len) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = Elem<T>::pack(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+            v.y = Elem<T>::pack(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            v.z = Elem<T>::pack(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+            v.w = Elem<T>::pack(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c + i) = v;
+          }
+        }
+      }
+      if (g == 0 && qi < q_len && p.lse != nullptr)
+        p.lse[static_cast<size_t>(q_start + qi) * p.HQ + h] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    }
   }
 
   tc_fence_before();
@@ -1121,15 +879,6 @@ __global__ void __launch_bounds__(TcCfg<HD>::kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-  if (p.sched != nullptr && threadIdx.x == 0) {
-    // the last CTA out leaves the counter zero for the next launch on this stream
-    __threadfence();
-    if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
-      p.sched[0] = 0u;
-      p.sched[1] = 0u;
-      __threadfence();
-    }
   }
 }
 
