@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -425,6 +426,7 @@ void plan_splits(int B, int HKV, int row_groups, int max_len, int* np_out, int* 
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
 
 template <int HD>
 int launch_packed_combine(const float* ows, const float* mdws, float* packed, int rows, int NP, cudaStream_t st) {
@@ -501,6 +503,8 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(out) & 7))
     return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned (out 8-byte)");
+  const long long rows = static_cast<long long>(B) * Sq * HQ;
+  if (rows > INT_MAX) return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows (B*Sq*HQ) above 2^31-1", rows);
   DecodeParams p{};
   p.q = q;
   p.k = k_cache;
@@ -534,7 +538,6 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
     p.c_len = max_len;
     return run_decode(p, D, bf16 != 0, st, kv_fp8);
   }
-  const long long rows = static_cast<long long>(B) * Sq * HQ;
   const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
@@ -711,16 +714,22 @@ static int cp_decode_impl(const void* q, const void* k_cache, const void* v_cach
     return fail(MXFA_ERR_UNSUPPORTED, "context-parallel decode covers up to 16 query heads per KV head");
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (B <= 0) return MXFA_OK;
+  if (PS <= 0 || num_pages <= 0) return fail(MXFA_ERR_INVALID, "bad cache geometry");
+  if (block_table != nullptr && BTW <= 0) return fail(MXFA_ERR_INVALID, "block table width must be positive");
+  if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(out) & 7) ||
+      !aligned16(local_buf))
+    return fail(MXFA_ERR_INVALID, "tensors and the exchange buffer must be 16-byte aligned (out 8-byte)");
+  const long long rows = static_cast<long long>(B) * HQ;
+  if (rows > INT_MAX) return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows (B*HQ) above 2^31-1", rows);
   const int max_len = block_table ? BTW * PS : PS;
   if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, 1, HQ, HKV, D, max_len, &num_splits, &chunk_len);
-  const long long rows = static_cast<long long>(B) * HQ;
   const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(MXFA_ERR_INVALID, "split workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
   if (static_cast<long long>(num_splits) * chunk_len < max_len)
     return fail(MXFA_ERR_INVALID, "%d splits of %d positions do not cover the cache capacity %d", num_splits,
                 chunk_len, max_len);
-  if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   DecodeParams p{};
   p.q = q;
   p.k = k_cache;
@@ -907,6 +916,9 @@ int mxfa_split_combine_launch(const float* ows, const float* mdws, void* out, fl
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (rows < 0 || NP < 1 || !ows || !mdws) return fail(MXFA_ERR_INVALID, "invalid combine argument");
   if (!aligned16(ows)) return fail(MXFA_ERR_INVALID, "ows must be 16-byte aligned");
+  // output pairs are written as 4-byte words, (m, d) pairs read as floats
+  if (!aligned4(mdws) || !aligned4(out) || !aligned4(out_f32) || !aligned4(lse))
+    return fail(MXFA_ERR_INVALID, "mdws, out, out_f32 and lse must be 4-byte aligned");
   return run_combine<false>(ows, mdws, out, out_f32, lse, rows, D, NP, bf16 != 0,
                             static_cast<cudaStream_t>(stream));
 }
@@ -915,6 +927,8 @@ int mxfa_lse_merge_launch(const float* packed, void* out, float* lse, int N, int
                           void* stream) {
   if (D != 64 && D != 128) return fail(MXFA_ERR_UNSUPPORTED, "head dim %d not in {64, 128}", D);
   if (rows < 0 || N < 1 || !packed || !out) return fail(MXFA_ERR_INVALID, "invalid merge argument");
+  if (!aligned4(packed) || !aligned4(out) || !aligned4(lse))
+    return fail(MXFA_ERR_INVALID, "packed, out and lse must be 4-byte aligned");
   return run_combine<true>(packed, nullptr, out, nullptr, lse, rows, D, N, bf16 != 0,
                            static_cast<cudaStream_t>(stream));
 }
@@ -967,10 +981,12 @@ static int varlen_fwd_impl(const void* q, const void* k, const void* v, const in
   if ((cu_q == nullptr) != (cu_k == nullptr)) return fail(MXFA_ERR_INVALID, "cu_q and cu_k must both be given");
   if (B == 0 || max_q == 0 || total_q == 0) return MXFA_OK;
   if (total_q < 0 || total_k <= 0) return fail(MXFA_ERR_INVALID, "total token counts must be positive");
-  if (cu_q == nullptr && (total_q != B * max_q || total_k != B * max_k))
+  if (cu_q == nullptr && (total_q != static_cast<long long>(B) * max_q || total_k != static_cast<long long>(B) * max_k))
     return fail(MXFA_ERR_INVALID, "dense layout needs total_q = B*max_q and total_k = B*max_k");
   if (!q || !k || !v || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
+  // the epilogue writes each output row in 16-byte stores
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
   if (HQ > 65535 || B > 65535) return fail(MXFA_ERR_UNSUPPORTED, "grid too large");
   PrefillParams p{};
   p.q = q;

@@ -74,3 +74,35 @@ def test_workspace_and_plan_are_host_only(lib):
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(_lib.NativeLibraryError, match="not built"):
         _lib.load(str(tmp_path / "libmxfa_b200.so"))
+
+
+def test_guards_refuse_bad_geometry_and_alignment_before_any_device_work(lib):
+    """Every entry refuses, on the host, what its kernels could not address: a zero page size or an
+    unaligned operand on the context-parallel decode, query rows past 2^31-1, an unaligned output on
+    the prefill (written in 16-byte stores) and unaligned combine operands. The addresses are never
+    dereferenced: each call returns before it touches a device."""
+    A = 1 << 20  # a 16-byte aligned stand-in address
+    inv, uns = _lib.MXFA_ERR_INVALID, _lib.MXFA_ERR_UNSUPPORTED
+
+    def cp(q=A, ps=16, btw=4, pages=10, local=None):
+        args = [q, A, A, A, A, A, A, A, 1 << 30, A, A]
+        if local is not None:
+            args.append(local)
+        args += [0, 2, 4, 32, 8, 128, ps, btw, pages, 0, 0, 1, 0.1, None]
+        fn = lib.mxfa_cp_attention_launch if local is not None else lib.mxfa_cp_decode_launch
+        return fn(*args)
+
+    assert cp(ps=0) == inv
+    assert cp(pages=0) == inv
+    assert cp(btw=0) == inv
+    assert cp(q=A + 8) == inv
+    assert cp(local=A + 8) == inv
+    rc = lib.mxfa_kvcache_attention_launch(A, A, A, A, A, A, A, A, 1 << 30, 1 << 16, 256, 256, 32, 128, 16, 4, 10,
+                                           0, 0, 0, 0, 1, 0.1, None)
+    assert rc == uns and b"2^31-1" in lib.mxfa_last_error()
+    rc = lib.mxfa_varlen_fwd_launch(A, A, A, None, None, A + 8, None, 2, 64, 64, 128, 128, 8, 2, 128, 1, 1, 0.1,
+                                    None)
+    assert rc == inv and b"aligned" in lib.mxfa_last_error()
+    assert lib.mxfa_split_combine_launch(A, A + 2, A, None, None, 4, 128, 2, 1, None) == inv
+    assert lib.mxfa_split_combine_launch(A, A, A + 2, None, None, 4, 128, 2, 1, None) == inv
+    assert lib.mxfa_lse_merge_launch(A + 2, A, None, 2, 4, 128, 1, None) == inv
