@@ -428,6 +428,15 @@ void plan_splits(int B, int HKV, int row_groups, int max_len, int* np_out, int* 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
 
+// Positions a sequence can hold (block-table width x page size, or one page
+// without a table); positions are 32-bit indices in the kernels.
+int cache_capacity(const void* block_table, int BTW, int PS, int* cap) {
+  const long long c = block_table ? static_cast<long long>(BTW) * PS : PS;
+  if (c > INT_MAX) return fail(MXFA_ERR_UNSUPPORTED, "cache capacity %lld positions above 2^31-1", c);
+  *cap = static_cast<int>(c);
+  return MXFA_OK;
+}
+
 template <int HD>
 int launch_packed_combine(const float* ows, const float* mdws, float* packed, int rows, int NP, cudaStream_t st) {
   if (rows == 0) return MXFA_OK;
@@ -528,7 +537,8 @@ static int kvcache_attention_impl(const void* q, const void* k_cache, const void
   p.k_new = k_new;
   p.v_new = v_new;
   p.order = order;
-  const int max_len = block_table ? BTW * PS : PS;
+  int max_len = 0;
+  if (int rc = cache_capacity(block_table, BTW, PS, &max_len)) return rc;
   if (num_splits <= 0 || chunk_len <= 0) {
     mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
   }
@@ -722,7 +732,8 @@ static int cp_decode_impl(const void* q, const void* k_cache, const void* v_cach
     return fail(MXFA_ERR_INVALID, "tensors and the exchange buffer must be 16-byte aligned (out 8-byte)");
   const long long rows = static_cast<long long>(B) * HQ;
   if (rows > INT_MAX) return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows (B*HQ) above 2^31-1", rows);
-  const int max_len = block_table ? BTW * PS : PS;
+  int max_len = 0;
+  if (int rc = cache_capacity(block_table, BTW, PS, &max_len)) return rc;
   if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, 1, HQ, HKV, D, max_len, &num_splits, &chunk_len);
   const size_t need = mxfa_split_workspace_bytes(static_cast<int>(rows), D, num_splits);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
@@ -877,7 +888,8 @@ int mxfa_kvcache_attention_packed_launch(const void* q, const void* k_cache, con
   if (!q || !k_cache || !v_cache || !seqlens || !packed) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache))
     return fail(MXFA_ERR_INVALID, "tensors must be 16-byte aligned");
-  const int max_len = block_table ? BTW * PS : PS;
+  int max_len = 0;
+  if (int rc = cache_capacity(block_table, BTW, PS, &max_len)) return rc;
   if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, 1, HQ, HKV, D, max_len, &num_splits, &chunk_len);
   if (static_cast<long long>(num_splits) * chunk_len < max_len)
     return fail(MXFA_ERR_INVALID, "%d splits of %d positions do not cover the cache capacity %d", num_splits,
@@ -1155,7 +1167,8 @@ extern "C" int mxfa_kvcache_attention_noalloc_launch(const void* q, const void* 
   if (!q || !k_cache || !v_cache || !seqlens || !out) return fail(MXFA_ERR_INVALID, "null tensor pointer");
   const long long rows = static_cast<long long>(B) * Sq * HQ;
   if (rows > 0x7FFFFFFFll) return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows exceed the 32-bit row index", rows);
-  const int max_len = block_table ? BTW * PS : PS;
+  int max_len = 0;
+  if (int rc = cache_capacity(block_table, BTW, PS, &max_len)) return rc;
   if (num_splits <= 0 || chunk_len <= 0) mxfa_kvcache_plan(B, Sq, HQ, HKV, D, max_len, &num_splits, &chunk_len);
   float* scratch = nullptr;
   if (num_splits > 1) {

@@ -100,6 +100,12 @@ def test_guards_refuse_bad_geometry_and_alignment_before_any_device_work(lib):
     rc = lib.mxfa_kvcache_attention_launch(A, A, A, A, A, A, A, A, 1 << 30, 1 << 16, 256, 256, 32, 128, 16, 4, 10,
                                            0, 0, 0, 0, 1, 0.1, None)
     assert rc == uns and b"2^31-1" in lib.mxfa_last_error()
+    rc = lib.mxfa_kvcache_attention_launch(A, A, A, A, A, A, A, A, 1 << 30, 1, 1, 32, 8, 128, 4096, 1 << 20, 10,
+                                           0, 0, 0, 0, 1, 0.1, None)
+    assert rc == uns and b"capacity" in lib.mxfa_last_error()
+    rc = lib.mxfa_kvcache_attention_noalloc_launch(A, A, A, A, A, A, A, 1, 1, 32, 8, 128, 4096, 1 << 20, 10, 0, 0,
+                                                   0, 0, 1, 0.1, None)
+    assert rc == uns and b"capacity" in lib.mxfa_last_error()
     rc = lib.mxfa_varlen_fwd_launch(A, A, A, None, None, A + 8, None, 2, 64, 64, 128, 128, 8, 2, 128, 1, 1, 0.1,
                                     None)
     assert rc == inv and b"aligned" in lib.mxfa_last_error()
