@@ -32,6 +32,11 @@ def test_header_and_binding_agree():
     assert declared_symbols() == sorted(_lib.SIGNATURES)
 
 
+def test_integration_guide_names_every_declared_symbol():
+    guide = open(os.path.join(os.path.dirname(HEADER), os.pardir, "INTEGRATION.md")).read()
+    assert [name for name in declared_symbols() if name not in guide] == []
+
+
 def test_library_exports_every_declared_symbol(lib):
     for name in declared_symbols():
         assert hasattr(lib, name), name
