@@ -158,6 +158,71 @@ def context_parallel_decode(q, k_cache, v_cache, local_seqlens, local_block_tabl
 
 # ------------------------------------------------- fused exchange (peer memory)
 
+
+_IPC_HANDLE_BYTES = 64  # sizeof(cudaIpcMemHandle_t)
+
+
+def map_exchange_buffers(lib, nbytes: int, world: int, rank: int, group=None):
+    """Allocate this rank's exchange buffer, export it and map every peer's (collective, current device).
+
+    Every rank takes the same collective steps whatever fails: the exported
+    handles are all-gathered (None from a rank whose allocation or export
+    failed), then every rank's import status.  A failure on any rank makes
+    every rank unmap and free what it holds and raise, instead of leaving the
+    other ranks blocked in their next collective.
+    Returns (this rank's buffer address, the peer mappings it opened, the
+    buffer address of every rank in rank order).
+    """
+    import ctypes
+
+    import torch.distributed as dist
+
+    from . import _lib
+
+    def status(rc, what):
+        if rc != _lib.MXFA_OK:
+            raise _lib.NativeLibraryError(f"{what}: status {rc}: {lib.mxfa_last_error().decode(errors='replace')}")
+
+    local, handle, error = None, None, None
+    try:
+        addr = ctypes.c_void_p()
+        status(lib.mxfa_peer_alloc(nbytes, ctypes.byref(addr)), "mxfa_peer_alloc")
+        local = addr.value
+        buf = (ctypes.c_char * _IPC_HANDLE_BYTES)()
+        status(lib.mxfa_peer_export(local, buf), "mxfa_peer_export")
+        handle = bytes(buf)
+    except Exception as exc:  # reported to every rank below
+        error = exc
+    handles = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    imported, ptrs = [], []
+    if error is None and all(h is not None for h in handles):
+        try:
+            for r, h in enumerate(handles):
+                if r == rank:
+                    ptrs.append(local)
+                    continue
+                peer = ctypes.c_void_p()
+                status(lib.mxfa_peer_import((ctypes.c_char * _IPC_HANDLE_BYTES).from_buffer_copy(h),
+                                            ctypes.byref(peer)), "mxfa_peer_import")
+                imported.append(peer.value)
+                ptrs.append(peer.value)
+        except Exception as exc:
+            error = exc
+    oks = [None] * world
+    dist.all_gather_object(oks, error is None, group=group)
+    if all(oks):
+        return local, imported, ptrs
+    for p in imported:
+        lib.mxfa_peer_close(p)
+    dist.barrier(group=group)  # no rank still maps a buffer that is about to be freed
+    if local is not None:
+        lib.mxfa_peer_free(local)
+    failed = [r for r, ok in enumerate(oks) if not ok]
+    raise RuntimeError(f"context-parallel exchange buffers could not be mapped: failed on rank(s) {failed}"
+                       + (f" ({error})" if error is not None else "")) from error
+
+
 class FusedContextParallelDecode:
     """Context-split decode with the (O, LSE) exchange fused into the kernels.
 
@@ -175,8 +240,6 @@ class FusedContextParallelDecode:
 
     def __init__(self, batch: int, q_heads: int, kv_heads: int, head_dim: int, *, group=None, device=None,
                  one_launch: bool = True):
-        import ctypes
-
         import torch
         import torch.distributed as dist
 
@@ -194,24 +257,7 @@ class FusedContextParallelDecode:
         if nbytes == 0:
             raise ValueError(f"unsupported context-parallel geometry {self.geometry}")
         with torch.cuda.device(self.device):
-            local = ctypes.c_void_p()
-            _lib.check(lib.mxfa_peer_alloc(nbytes, ctypes.byref(local)), "mxfa_peer_alloc")
-            self._local = local.value
-            handle = (ctypes.c_char * 64)()
-            _lib.check(lib.mxfa_peer_export(self._local, handle), "mxfa_peer_export")
-            handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(handle), group=group)
-            self._imported = []
-            ptrs = []
-            for r, h in enumerate(handles):
-                if r == self.rank:
-                    ptrs.append(self._local)
-                    continue
-                buf = (ctypes.c_char * 64).from_buffer_copy(h)
-                peer = ctypes.c_void_p()
-                _lib.check(lib.mxfa_peer_import(buf, ctypes.byref(peer)), "mxfa_peer_import")
-                self._imported.append(peer.value)
-                ptrs.append(peer.value)
+            self._local, self._imported, ptrs = map_exchange_buffers(lib, nbytes, self.world, self.rank, group)
             # device array of the peers' buffer addresses (uint64 stored as int64)
             self.peer_table = torch.tensor([p - (1 << 64) if p >= (1 << 63) else p for p in ptrs],
                                            dtype=torch.int64, device=self.device)

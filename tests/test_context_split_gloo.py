@@ -9,6 +9,7 @@ context.  No GPU is used: the CUDA halves are covered by the -m gpu tests.
 
 from __future__ import annotations
 
+import ctypes
 import datetime
 import math
 import socket
@@ -110,3 +111,90 @@ def test_context_split_exchange_and_merge_over_gloo(world):
         err, lerr, shape = result[rank]
         assert shape == (world, 3 * 8, 65)
         assert err < 1e-5 and lerr < 1e-5 and math.isfinite(err)
+
+
+class _FakePeerLib:
+    """The library's peer-memory entries for CPU ranks: addresses are integers, a handle carries the exporting
+    rank's address, and `fail_at` = (rank, step) makes that rank's step return a CUDA error status."""
+
+    def __init__(self, rank, fail_at):
+        self.rank, self.fail_at = rank, fail_at
+        self.log = []
+
+    def _fails(self, step):
+        return self.fail_at == (self.rank, step)
+
+    def mxfa_last_error(self):
+        return b"injected failure"
+
+    def mxfa_peer_alloc(self, nbytes, out):
+        if self._fails("alloc"):
+            return 3
+        out._obj.value = 0x100000 * (self.rank + 1)
+        self.log.append(("alloc", out._obj.value))
+        return 0
+
+    def mxfa_peer_export(self, ptr, handle):
+        if self._fails("export"):
+            return 3
+        ctypes.memmove(handle, int(ptr).to_bytes(8, "little") + bytes(56), 64)
+        return 0
+
+    def mxfa_peer_import(self, handle, out):
+        if self._fails("import"):
+            return 3
+        out._obj.value = int.from_bytes(bytes(handle)[:8], "little") + 0x1000  # this rank's mapping of it
+        self.log.append(("import", out._obj.value))
+        return 0
+
+    def mxfa_peer_close(self, ptr):
+        self.log.append(("close", ptr))
+        return 0
+
+    def mxfa_peer_free(self, ptr):
+        self.log.append(("free", ptr))
+        return 0
+
+
+def _mapping_worker(rank, world, port, fail_at, result):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        lib = _FakePeerLib(rank, fail_at)
+        try:
+            local, imported, ptrs = cs.map_exchange_buffers(lib, 4096, world, rank)
+            result[rank] = ("mapped", local, imported, ptrs, lib.log)
+        except RuntimeError as exc:
+            result[rank] = ("raised", str(exc), lib.log)
+        dist.barrier()  # still in step with the other ranks after either outcome
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_at", [None, (1, "alloc"), (2, "export"), (0, "import")])
+def test_exchange_buffer_mapping_agrees_across_ranks(fail_at):
+    """Every rank maps every peer's buffer, or, when one rank's allocation, export or import fails, every rank
+    raises naming that rank and releases all it mapped and allocated (no rank is left waiting)."""
+    import torch.multiprocessing as mp
+
+    world = 3
+    result = mp.Manager().dict()
+    mp.spawn(_mapping_worker, args=(world, _free_port(), fail_at, result), nprocs=world, join=True)
+    assert sorted(result.keys()) == list(range(world))
+    for rank in range(world):
+        outcome = result[rank]
+        if fail_at is None:
+            _, local, imported, ptrs, _ = outcome
+            assert outcome[0] == "mapped" and local == 0x100000 * (rank + 1) and ptrs[rank] == local
+            assert ptrs == [0x100000 * (r + 1) + (0 if r == rank else 0x1000) for r in range(world)]
+            assert imported == [p for r, p in enumerate(ptrs) if r != rank]
+            continue
+        status, message, log = outcome
+        assert status == "raised" and f"rank(s) [{fail_at[0]}]" in message
+        opened = [p for step, p in log if step == "import"]
+        allocated = [p for step, p in log if step == "alloc"]
+        assert sorted(p for step, p in log if step == "close") == sorted(opened)
+        assert [p for step, p in log if step == "free"] == allocated
+        assert len(allocated) == (0 if fail_at == (rank, "alloc") else 1)
