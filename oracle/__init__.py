@@ -12,6 +12,10 @@ algorithm of the reference's PyTorch oracle ``mxflashattn/reference.py``:
 * ``attention_batched``  -> reference.py:43-57
 * ``attention_varlen``   -> reference.py:60-85
 * ``attention_kvcache``  -> reference.py:88-139 (paged/dense append + gather)
+* ``attention_chunked``, ``attention_chunked_fallback`` -> the chunked
+  online-softmax prototype ``mxflashattn/prefill.py:11-108`` (a second
+  oracle for the online softmax; pinned by ``tests/golden/chunked.npz``,
+  which ``tests/golden/make_chunked_golden.py`` produced by running it)
 
 The reference returns no log-sum-exp; ``lse`` here is the harness addition
 the split-KV merge needs (natural-log logsumexp of the scaled scores, the
@@ -24,6 +28,8 @@ produced by importing and running the reference implementation itself.
 
 from .attention import (
     attention_batched,
+    attention_chunked,
+    attention_chunked_fallback,
     attention_kvcache,
     attention_single,
     attention_varlen,
@@ -35,6 +41,8 @@ from .attention import (
 __all__ = [
     "attention_single",
     "attention_batched",
+    "attention_chunked",
+    "attention_chunked_fallback",
     "attention_varlen",
     "attention_kvcache",
     "gather_paged_kv",

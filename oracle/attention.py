@@ -222,3 +222,52 @@ def merge_partials(o, m, d):
     out = (w[:, None] * o).sum(axis=0) / den if den > 0 else np.zeros(o.shape[1])
     lse = (mm + math.log2(den)) * LN2 if den > 0 else -np.inf
     return out, lse
+
+
+def attention_chunked(q, k, v, *, chunk_size=256, softmax_scale=None, causal=False):
+    """Online-softmax attention over key chunks, float32 (prefill.py:11-81).
+
+    ``q`` [B, Sq, HQ, D], ``k``/``v`` [B, Sk, HKV, D] (GQA: each KV head serves
+    ``HQ // HKV`` consecutive query heads).  Keys are visited in chunks of
+    ``chunk_size``; each row keeps a running maximum ``m``, normaliser ``l``
+    and unnormalised output ``o``, and a chunk rescales them by
+    ``exp(m_old - m_new)`` before adding its own ``exp(s - m_new)`` terms.
+    Causal masking is bottom-right aligned like the direct oracle; a row whose
+    keys are all masked so far contributes nothing, and a row that never sees
+    a key outputs 0.  The second oracle for the online softmax the kernels
+    run: it must agree with ``attention_batched`` to float32 rounding.
+    """
+    if not isinstance(chunk_size, (int, np.integer)) or chunk_size <= 0:
+        raise ValueError("chunk_size must be a positive integer")
+    B, Sq, HQ, D = q.shape
+    Sk, HKV = k.shape[1], k.shape[2]
+    scale = np.float32(_scale(D, softmax_scale))
+    G = HQ // HKV
+    qf = q.astype(np.float32).transpose(0, 2, 1, 3)                          # [B, HQ, Sq, D]
+    kf = np.repeat(k.astype(np.float32).transpose(0, 2, 1, 3), G, axis=1)   # [B, HQ, Sk, D]
+    vf = np.repeat(v.astype(np.float32).transpose(0, 2, 1, 3), G, axis=1)
+    o = np.zeros((B, HQ, Sq, D), np.float32)
+    l = np.zeros((B, HQ, Sq, 1), np.float32)
+    m = np.full((B, HQ, Sq, 1), -np.inf, np.float32)
+    row_pos = np.arange(Sq) + (Sk - Sq)  # the last key each query row may see
+    for lo in range(0, Sk, chunk_size):
+        hi = min(lo + chunk_size, Sk)
+        s = (qf @ kf[:, :, lo:hi].transpose(0, 1, 3, 2)) * scale          # [B, HQ, Sq, hi-lo]
+        if causal:
+            s = np.where(np.arange(lo, hi)[None, :] > row_pos[:, None], np.float32(-np.inf), s)
+        m_new = np.maximum(m, s.max(axis=-1, keepdims=True))
+        seen = np.isfinite(m_new)
+        keep = np.where(np.isfinite(m), np.exp(m - np.where(seen, m_new, 0.0)), 0.0).astype(np.float32)
+        p = np.where(np.isfinite(s), np.exp(s - np.where(seen, m_new, 0.0)), 0.0).astype(np.float32)
+        l = l * keep + p.sum(axis=-1, keepdims=True)
+        o = o * keep + p @ vf[:, :, lo:hi]
+        m = m_new
+    out = np.where(l > 0, o / np.where(l > 0, l, 1.0), 0.0).astype(np.float32)
+    return out.transpose(0, 2, 1, 3)
+
+
+def attention_chunked_fallback(q, k, v, *, chunk_size=256, softmax_scale=None, causal=False):
+    """The direct oracle when one chunk covers every key, else the chunked one (prefill.py:84-108)."""
+    if chunk_size >= k.shape[1]:
+        return attention_batched(q, k, v, softmax_scale=softmax_scale, causal=causal)
+    return attention_chunked(q, k, v, chunk_size=chunk_size, softmax_scale=softmax_scale, causal=causal)

@@ -74,3 +74,35 @@ def varlen_cases():
             204, q_lens=[2, 5], k_lens=[5, 3], q_heads=4, kv_heads=2, head_dim=64, dtype="fp16",
             causal=False, softmax_scale=0.0),
     }
+
+
+class ChunkedCase:
+    """Dense [B, S, H, D] inputs of a chunked-prefill golden and the chunk size it runs with."""
+
+    def __init__(self, base, batch: int, chunk_size: int):
+        self.q = base.q.reshape(batch, -1, *base.q.shape[1:])
+        self.k = base.k.reshape(batch, -1, *base.k.shape[1:])
+        self.v = base.v.reshape(batch, -1, *base.v.shape[1:])
+        self.dtype, self.softmax_scale, self.causal = base.dtype, base.softmax_scale, base.causal
+        self.chunk_size = chunk_size
+
+
+def chunked_cases():
+    """name -> ChunkedCase for the chunked online-softmax prototype (``prefill.py``) goldens."""
+    return {
+        "chunked_causal_bf16_c7": ChunkedCase(syn.varlen_case(
+            300, q_lens=[33, 33], q_heads=4, kv_heads=2, head_dim=64, dtype="bf16", causal=True), 2, 7),
+        "chunked_noncausal_fp16_k_longer_c64": ChunkedCase(syn.varlen_case(
+            301, q_lens=[5, 5], k_lens=[130, 130], q_heads=8, kv_heads=2, head_dim=128, dtype="fp16",
+            causal=False), 2, 64),
+        "chunked_causal_q_longer_than_k_c1": ChunkedCase(syn.varlen_case(
+            302, q_lens=[6], k_lens=[4], q_heads=2, kv_heads=1, head_dim=64, dtype="bf16", causal=True), 1, 1),
+        "chunked_causal_outliers_c16": ChunkedCase(syn.varlen_case(
+            303, q_lens=[48], q_heads=4, kv_heads=2, head_dim=128, dtype="bf16", causal=True,
+            outlier_frac=0.01), 1, 16),
+        "chunked_one_chunk_c256": ChunkedCase(syn.varlen_case(
+            304, q_lens=[40, 40, 40], q_heads=4, kv_heads=4, head_dim=64, dtype="fp16", causal=True), 3, 256),
+        "chunked_zero_scale_c3": ChunkedCase(syn.varlen_case(
+            305, q_lens=[4, 4], k_lens=[9, 9], q_heads=4, kv_heads=2, head_dim=64, dtype="fp16", causal=False,
+            softmax_scale=0.0), 2, 3),
+    }

@@ -8,6 +8,8 @@ dtype-cast result, the harness LSE and the bit-exact append placement.
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -86,3 +88,29 @@ def test_empty_split_merge_is_zero():
     d = np.zeros(3)
     out, lse = oracle.merge_partials(o, m, d)
     assert np.all(out == 0) and lse == -np.inf
+
+
+CHUNKED = golden_cases.chunked_cases()
+
+
+@pytest.fixture(scope="module")
+def chunked_golden():
+    with np.load(os.path.join(os.path.dirname(golden_cases.__file__), "chunked.npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("name", sorted(CHUNKED))
+def test_chunked_oracle_matches_the_reference_prototype(name, chunked_golden):
+    """The chunked online-softmax restatement against the reference's own prefill_chunked_reference outputs."""
+    case = CHUNKED[name]
+    assert chunked_golden[f"{name}.digest"].item() == golden_cases.digest(case.q, case.k, case.v)
+    kw = dict(chunk_size=case.chunk_size, softmax_scale=case.softmax_scale, causal=case.causal)
+    out = oracle.attention_chunked(case.q, case.k, case.v, **kw)
+    np.testing.assert_allclose(out, chunked_golden[f"{name}.out_f32"], rtol=1e-5, atol=2e-5)
+    cast = syn.round_dtype(out, case.dtype)
+    ref = chunked_golden[f"{name}.out"]
+    ulp = 2.0 ** -7 if case.dtype == "bf16" else 2.0 ** -10
+    assert np.all(np.abs(cast - ref) <= ulp * np.maximum(np.abs(ref), 1e-3) + 1e-6)
+    if f"{name}.fallback_f32" in chunked_golden:
+        fb = oracle.attention_chunked_fallback(case.q, case.k, case.v, **kw)
+        np.testing.assert_allclose(fb, chunked_golden[f"{name}.fallback_f32"], rtol=1e-5, atol=2e-5)

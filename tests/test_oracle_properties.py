@@ -130,3 +130,19 @@ def test_causal_rows_see_the_bottom_right_aligned_prefix(seed, q_len, extra_keys
         hi = i + k_len - q_len + 1
         row = oracle.attention_single(q[i:i + 1], k[:hi], v[:hi], softmax_scale=0.3, precision=np.float64)
         np.testing.assert_allclose(causal[i], row[0], rtol=1e-12, atol=1e-13)
+
+
+@SETTINGS
+@given(seed=st.integers(0, 2**31 - 1), q_len=st.integers(1, 40), extra_keys=st.integers(-3, 60),
+       chunk=st.integers(1, 80), gq=st.sampled_from([1, 2, 4]), causal=st.booleans())
+def test_chunked_online_softmax_equals_the_direct_oracle(seed, q_len, extra_keys, chunk, gq, causal):
+    """The chunked prototype's restatement (prefill.py:11-81) against attention_batched, as the reference's own
+    prefill tests check it: any chunk size, GQA, causal rows with and without visible keys."""
+    rng = np.random.default_rng(seed)
+    k_len = max(1, q_len + extra_keys)
+    q = rng.standard_normal((2, q_len, 2 * gq, 32)).astype(np.float32)
+    k = (rng.standard_normal((2, k_len, 2, 32)) * 1.5).astype(np.float32)
+    v = rng.standard_normal((2, k_len, 2, 32)).astype(np.float32)
+    chunked = oracle.attention_chunked(q, k, v, chunk_size=chunk, softmax_scale=0.2, causal=causal)
+    direct = oracle.attention_batched(q, k, v, softmax_scale=0.2, causal=causal)
+    np.testing.assert_allclose(chunked, direct, rtol=2e-5, atol=2e-5)
