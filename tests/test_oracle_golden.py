@@ -114,3 +114,20 @@ def test_chunked_oracle_matches_the_reference_prototype(name, chunked_golden):
     if f"{name}.fallback_f32" in chunked_golden:
         fb = oracle.attention_chunked_fallback(case.q, case.k, case.v, **kw)
         np.testing.assert_allclose(fb, chunked_golden[f"{name}.fallback_f32"], rtol=1e-5, atol=2e-5)
+
+
+def test_chunked_fallback_takes_the_direct_oracle_for_one_chunk():
+    """One chunk covering every key runs attention_batched itself (prefill.py:98-99)."""
+    case = CHUNKED["chunked_one_chunk_c256"]
+    fb = oracle.attention_chunked_fallback(case.q, case.k, case.v, chunk_size=case.k.shape[1],
+                                           softmax_scale=case.softmax_scale, causal=case.causal)
+    direct = oracle.attention_batched(case.q, case.k, case.v, softmax_scale=case.softmax_scale, causal=case.causal)
+    assert np.array_equal(fb, direct)
+
+
+@pytest.mark.parametrize("chunk_size", [0, -4, 2.5])
+def test_chunked_oracle_rejects_invalid_chunk_sizes(chunk_size):
+    """A chunk size that is not a positive integer is refused (prefill.py:28-29)."""
+    case = CHUNKED["chunked_causal_bf16_c7"]
+    with pytest.raises(ValueError, match="chunk_size must be a positive integer"):
+        oracle.attention_chunked(case.q, case.k, case.v, chunk_size=chunk_size)
