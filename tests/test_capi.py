@@ -32,6 +32,53 @@ def test_header_and_binding_agree():
     assert declared_symbols() == sorted(_lib.SIGNATURES)
 
 
+def _prototypes():
+    """name -> (return type, [parameter types]) parsed from the header's declarations."""
+    text = re.sub(r"/\*.*?\*/|//[^\n]*", " ", open(HEADER).read(), flags=re.S)
+    text = re.sub(r"^\s*#.*$", ";", text, flags=re.M)  # preprocessor lines end a declaration
+    text = re.sub(r'extern\s+"C"\s*\{|\}', ";", text)
+    protos = {}
+    for ret, name, params in re.findall(r"(?<=;)\s*([A-Za-z_][\w\s]*?\**)\s*\b(mxfa_[a-z0-9_]+)\s*\(([^)]*)\)\s*;",
+                                        text):
+        params = " ".join(params.split())
+        types = [] if params in ("", "void") else [re.sub(r"\s*\b\w+$", "", a.strip()) for a in params.split(",")]
+        protos[name] = (" ".join(ret.split()), types)
+    return protos
+
+
+def _kind(c_type: str) -> str:
+    if "*" in c_type:
+        return "pointer"
+    return {"int": "int", "float": "float", "size_t": "size_t"}[c_type.replace("const ", "").strip()]
+
+
+def _ctypes_kind(t) -> str:
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(t, "_type_") and isinstance(t._type_, type):
+        return "pointer"
+    return {ctypes.c_int: "int", ctypes.c_float: "float", ctypes.c_size_t: "size_t"}[t]
+
+
+def test_binding_argument_lists_match_the_header_prototypes():
+    """Every ctypes signature has the header's parameter count and kinds (pointer / int / float / size_t) and
+    return kind, so an argument added on one side only cannot shift the others."""
+    protos = _prototypes()
+    assert sorted(protos) == declared_symbols()
+    for name, (restype, argtypes) in _lib.SIGNATURES.items():
+        ret, params = protos[name]
+        assert [_kind(p) for p in params] == [_ctypes_kind(a) for a in argtypes], name
+        assert _kind(ret) == _ctypes_kind(restype), name
+
+
+def test_status_codes_and_flags_match_the_header():
+    text = open(HEADER).read()
+    defines = {k: int(v.rstrip("u"), 0) for k, v in re.findall(r"#define (MXFA_\w+) \(?(-?\w+)\)?", text)
+               if re.fullmatch(r"-?(0x[0-9a-fA-F]+|\d+)u?", v)}
+    for name in ("MXFA_OK", "MXFA_ERR_UNSUPPORTED", "MXFA_ERR_INVALID", "MXFA_ERR_CUDA"):
+        assert getattr(_lib, name) == defines[name], name
+    for name in ("PAGE_OUT_OF_RANGE", "TABLE_TOO_NARROW", "WAIT_TIMEOUT", "DENSE_OVERFLOW", "BAD_ORDER"):
+        assert getattr(_lib, f"FLAG_{name}") == defines[f"MXFA_FLAG_{name}"], name
+
+
 def test_integration_guide_names_every_declared_symbol():
     guide = open(os.path.join(os.path.dirname(HEADER), os.pardir, "INTEGRATION.md")).read()
     assert [name for name in declared_symbols() if name not in guide] == []
