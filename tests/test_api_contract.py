@@ -289,3 +289,21 @@ def test_length_order_helper_guards():
         kvcache_length_order(torch.zeros(2, 2, dtype=torch.int32))
     with pytest.raises(ValueError, match="CUDA device"):
         kvcache_length_order(torch.zeros(4, dtype=torch.int32))
+
+
+def test_public_signatures_are_the_references():
+    """Each public function takes the reference's parameters in its order, with its kinds and defaults
+    (tests/golden/api_signatures.json, read from the reference's api.py); additions are keyword-only."""
+    import inspect
+    import json
+    import os
+
+    import mxflashattn_b200.api as api
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "api_signatures.json")
+    with open(path) as f:
+        reference = json.load(f)
+    for name, ref_params in reference.items():
+        ours = [[n, p.kind.name, repr(p.default)] for n, p in inspect.signature(getattr(api, name)).parameters.items()]
+        assert ours[:len(ref_params)] == ref_params, name
+        assert all(kind == "KEYWORD_ONLY" for _, kind, _ in ours[len(ref_params):]), name
