@@ -307,3 +307,30 @@ def test_public_signatures_are_the_references():
         ours = [[n, p.kind.name, repr(p.default)] for n, p in inspect.signature(getattr(api, name)).parameters.items()]
         assert ours[:len(ref_params)] == ref_params, name
         assert all(kind == "KEYWORD_ONLY" for _, kind, _ in ours[len(ref_params):]), name
+
+
+def _reference_errors():
+    import json
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "api_errors.json")
+    with open(path) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("case", sorted(_reference_errors()))
+def test_invalid_calls_raise_what_the_reference_raises(case, monkeypatch):
+    """Exception type and message on the reference's invalid calls (tests/golden/api_errors.json, recorded by
+    running the reference's API on tests/golden/api_error_cases.py)."""
+    import api_error_cases
+
+    import mxflashattn_b200
+
+    fn_name, build, strict = api_error_cases.cases()[case]
+    monkeypatch.setenv("MXFLASHATTN_STRICT_VALIDATION", "1" if strict else "0")
+    monkeypatch.delenv("MXFLASHATTN_ALLOW_FALLBACK", raising=False)
+    args, kwargs = build()
+    expected_type, expected_message = _reference_errors()[case]
+    with pytest.raises(Exception) as info:
+        getattr(mxflashattn_b200, fn_name)(*args, **kwargs)
+    assert [type(info.value).__name__, str(info.value)] == [expected_type, expected_message]
