@@ -4,15 +4,19 @@ Usage (in a container where the reference checkout is present):
 
     python tests/golden/make_api_signatures.py [--reference-root PATH]
 
-It imports ``mxflashattn/api.py`` of the MXFlashAttn checkout and writes, for
-``flash_attn_func``, ``flash_attn_varlen_func`` and ``flash_attn_with_kvcache``,
-each parameter's name, kind and default (as ``repr``) in order to
-``tests/golden/api_signatures.json``.
+It imports the MXFlashAttn checkout's package and writes to
+``tests/golden/api_signatures.json``, for ``flash_attn_func``,
+``flash_attn_varlen_func`` and ``flash_attn_with_kvcache``, each parameter's
+name, kind and default (as ``repr``) in order, and, for the records and
+policy objects the package exports (``DispatchInfo``, ``ErrorSummary``,
+``DispatchPolicyConfig``, ``WorkloadShape``, ``DispatchDecision``), each
+field's name and default in order.
 """
 
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import inspect
 import json
 import os
@@ -20,10 +24,15 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 FUNCTIONS = ("flash_attn_func", "flash_attn_varlen_func", "flash_attn_with_kvcache")
+RECORDS = ("DispatchInfo", "ErrorSummary", "DispatchPolicyConfig", "WorkloadShape", "DispatchDecision")
 
 
 def describe(fn) -> list[list[str]]:
     return [[name, p.kind.name, repr(p.default)] for name, p in inspect.signature(fn).parameters.items()]
+
+
+def fields(cls) -> list[list[str | None]]:
+    return [[f.name, None if f.default is dataclasses.MISSING else repr(f.default)] for f in dataclasses.fields(cls)]
 
 
 def main() -> None:
@@ -35,10 +44,13 @@ def main() -> None:
     if not args.reference_root:
         parser.error("--reference-root (or MXFA_REFERENCE_ROOT) is required")
     sys.path.insert(0, args.reference_root)
-    from mxflashattn import api  # the reference's public API
+    import mxflashattn  # the reference's public package
+    from mxflashattn import api
 
+    record = {name: describe(getattr(api, name)) for name in FUNCTIONS}
+    record["records"] = {name: fields(getattr(mxflashattn, name)) for name in RECORDS}
     with open(args.out, "w") as f:
-        json.dump({name: describe(getattr(api, name)) for name in FUNCTIONS}, f, indent=1)
+        json.dump(record, f, indent=1)
         f.write("\n")
     print(f"wrote {args.out}")
 

@@ -292,17 +292,25 @@ def test_length_order_helper_guards():
 
 
 def test_public_signatures_are_the_references():
-    """Each public function takes the reference's parameters in its order, with its kinds and defaults
-    (tests/golden/api_signatures.json, read from the reference's api.py); additions are keyword-only."""
+    """Each public function takes the reference's parameters in its order, with its kinds and defaults, and each
+    exported record has its fields and defaults (tests/golden/api_signatures.json, read from the reference
+    package); additions to the functions are keyword-only."""
+    import dataclasses
     import inspect
     import json
     import os
 
+    import mxflashattn_b200
     import mxflashattn_b200.api as api
 
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "api_signatures.json")
     with open(path) as f:
         reference = json.load(f)
+    records = reference.pop("records")
+    for name, ref_fields in records.items():
+        ours = [[f.name, None if f.default is dataclasses.MISSING else repr(f.default)]
+                for f in dataclasses.fields(getattr(mxflashattn_b200, name))]
+        assert ours == ref_fields, name
     for name, ref_params in reference.items():
         ours = [[n, p.kind.name, repr(p.default)] for n, p in inspect.signature(getattr(api, name)).parameters.items()]
         assert ours[:len(ref_params)] == ref_params, name
