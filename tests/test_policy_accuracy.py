@@ -59,3 +59,39 @@ def test_error_summary_nonfinite_and_invalid():
         summarize_error(torch.empty(0), torch.empty(0))
     with pytest.raises(ValueError, match="identical shapes"):
         summarize_error(torch.zeros(2), torch.zeros(3))
+
+
+def _recorded_policy():
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "policy_decisions.json")) as f:
+        return json.load(f)
+
+
+def test_policy_decisions_on_the_threshold_grid_are_the_references():
+    """Every grid point straddling the thresholds (tests/golden/policy_grid.py) gets the decision the reference's
+    policy made there (tests/golden/policy_decisions.json, recorded by running it)."""
+    import policy_grid
+
+    recorded = _recorded_policy()
+    table = [tuple(row) for row in recorded["decisions"]]
+    points = list(policy_grid.grid())
+    assert len(points) == len(recorded["index"])
+    mismatches = []
+    for (c, phase, b, q, kv, d, g), code in zip(points, recorded["index"]):
+        dec = AdaptiveDispatchPolicy(DispatchPolicyConfig(**policy_grid.CONFIGS[c])).select(
+            WorkloadShape(phase, b, q, kv, d, g))
+        got = (dec.backend, dec.reason, dec.eligible, dec.policy_enabled, dec.thresholds_calibrated)
+        if got != table[ord(code) - ord("a")]:
+            mismatches.append(((c, phase, b, q, kv, d, g), got))
+    assert mismatches == []
+
+
+def test_invalid_workload_shapes_raise_what_the_reference_raises():
+    import policy_grid
+
+    for name, fields in policy_grid.invalid_shapes().items():
+        with pytest.raises(Exception) as info:
+            WorkloadShape(*fields)
+        assert [type(info.value).__name__, str(info.value)] == _recorded_policy()["invalid"][name], name
