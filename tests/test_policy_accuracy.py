@@ -95,3 +95,24 @@ def test_invalid_workload_shapes_raise_what_the_reference_raises():
         with pytest.raises(Exception) as info:
             WorkloadShape(*fields)
         assert [type(info.value).__name__, str(info.value)] == _recorded_policy()["invalid"][name], name
+
+
+@pytest.mark.parametrize("case", ["bf16_rounding", "small_noise", "zeros_expected", "one_nan", "one_inf", "fp16_pair",
+                                  "shape_mismatch", "empty", "not_a_tensor"])
+def test_error_reports_are_the_references(case):
+    """summarize_error's report, or its exception, on seeded inputs (tests/golden/accuracy_summaries.json,
+    recorded by running the reference's summarize_error)."""
+    import json
+    import os
+
+    import make_accuracy_summaries as gen
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "accuracy_summaries.json")) as f:
+        expected = json.load(f)[case]
+    ours = gen.report(summarize_error, case)
+    assert ours.keys() == expected.keys()
+    for key, value in expected.items():
+        if isinstance(value, float):
+            assert ours[key] == pytest.approx(value, rel=1e-6, abs=1e-12), key
+        else:
+            assert ours[key] == value, key
