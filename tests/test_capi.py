@@ -164,3 +164,29 @@ def test_guards_refuse_bad_geometry_and_alignment_before_any_device_work(lib):
     assert lib.mxfa_split_combine_launch(A, A + 2, A, None, None, 4, 128, 2, 1, None) == inv
     assert lib.mxfa_split_combine_launch(A, A, A + 2, None, None, 4, 128, 2, 1, None) == inv
     assert lib.mxfa_lse_merge_launch(A + 2, A, None, 2, 4, 128, 1, None) == inv
+
+
+def test_split_plan_invariants(lib):
+    """mxfa_kvcache_plan over random shapes: at least one split, chunks a multiple of the 16-token tile, the
+    splits cover the cache capacity with no empty trailing split, at most 1024 splits, and one split when the
+    capacity is 256 positions or fewer (host-only; the SM count falls back to 148 without a device)."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=300, deadline=None)
+    @given(b=st.integers(1, 4096), sq=st.integers(1, 16), hkv=st.sampled_from([1, 2, 4, 8, 16]),
+           gq=st.sampled_from([1, 2, 4, 8]), max_len=st.integers(0, 1 << 20))
+    def check(b, sq, hkv, gq, max_len):
+        np_, cl = ctypes.c_int(0), ctypes.c_int(0)
+        assert lib.mxfa_kvcache_plan(b, sq, hkv * gq, hkv, 128, max_len, ctypes.byref(np_), ctypes.byref(cl)) == 0
+        n, c = np_.value, cl.value
+        cap = max(max_len, 1)
+        assert n >= 1 and c >= 16 and c % 16 == 0
+        assert n * c >= cap and (n - 1) * c < cap
+        assert n <= 1024
+        if cap <= 256:
+            assert n == 1
+        rows = b * sq * hkv * gq
+        assert lib.mxfa_split_workspace_bytes(rows, 128, n) == rows * n * 130 * 4
+
+    check()
