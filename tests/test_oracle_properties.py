@@ -146,3 +146,23 @@ def test_chunked_online_softmax_equals_the_direct_oracle(seed, q_len, extra_keys
     chunked = oracle.attention_chunked(q, k, v, chunk_size=chunk, softmax_scale=0.2, causal=causal)
     direct = oracle.attention_batched(q, k, v, softmax_scale=0.2, causal=causal)
     np.testing.assert_allclose(chunked, direct, rtol=2e-5, atol=2e-5)
+
+
+def test_long_context_chunked_error_summary_is_stable():
+    """Causal self-attention over 128, 512 and 4096 tokens, chunk 64: the chunked oracle against the direct one
+    through the error report, at the bounds of the reference's long-context test (test_long_context_accuracy.py:
+    max 1e-4, p99 1e-5) plus a 4096-token case."""
+    import torch
+
+    from mxflashattn_b200.accuracy import summarize_error
+
+    for kv_len in (128, 512, 4096):
+        rng = np.random.default_rng(20261016 + kv_len)
+        q = rng.standard_normal((1, kv_len, 2, 64)).astype(np.float32)
+        k = rng.standard_normal((1, kv_len, 1, 64)).astype(np.float32)
+        v = rng.standard_normal((1, kv_len, 1, 64)).astype(np.float32)
+        chunked = oracle.attention_chunked(q, k, v, chunk_size=64, causal=True)
+        direct = oracle.attention_batched(q, k, v, causal=True)
+        summary = summarize_error(torch.from_numpy(chunked), torch.from_numpy(direct))
+        assert summary.finite
+        assert summary.max_abs < 1e-4 and summary.p99_abs < 1e-5, (kv_len, summary)
