@@ -12,10 +12,22 @@ non-zero status.  ``split_plan`` is the vLLM hook's NP / c_len heuristic
 from __future__ import annotations
 
 import os
+import re
 
 import torch
 
 from . import _lib
+
+
+def softmax_variant_from_env() -> int:
+    """``um`` as the reference binding reads it per call (m1_binding.cpp:100-105): 2 unless ``MXFA_M1_UM``
+    parses, the way C ``atoi`` does (leading blanks, sign, digits; 0 when there are none), to 0 or 1."""
+    env = os.getenv("MXFA_M1_UM")
+    if env is None:
+        return 2
+    m = re.match(r"[ \t\n\v\f\r]*([+-]?\d+)", env)
+    val = int(m.group(1)) if m else 0
+    return val if val in (0, 1) else 2
 
 
 def paged_decode_split(q, k, v, bt, sl, scale, stream, np, c_len):
@@ -39,15 +51,7 @@ def paged_decode_split(q, k, v, bt, sl, scale, stream, np, c_len):
     ows = torch.empty((B, HQ, np, D), device=q.device, dtype=torch.float32)
     mdws = torch.empty((B, HQ, np, 2), device=q.device, dtype=torch.float32)
     out = torch.empty((B, 1, HQ, D), device=q.device, dtype=q.dtype)
-    um = 2
-    env = os.getenv("MXFA_M1_UM")
-    if env is not None:
-        try:
-            val = int(env)
-        except ValueError:
-            val = 2
-        if val in (0, 1):
-            um = val
+    um = softmax_variant_from_env()
     with torch.cuda.device(q.device):
         rc = _lib.load().mxfa_paged_decode_split_launch(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), bt.data_ptr(), sl.data_ptr(), out.data_ptr(), ows.data_ptr(),

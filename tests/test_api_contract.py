@@ -342,3 +342,16 @@ def test_invalid_calls_raise_what_the_reference_raises(case, monkeypatch):
     with pytest.raises(Exception) as info:
         getattr(mxflashattn_b200, fn_name)(*args, **kwargs)
     assert [type(info.value).__name__, str(info.value)] == [expected_type, expected_message]
+
+
+@pytest.mark.parametrize("env,um", [(None, 2), ("0", 0), ("1", 1), ("2", 2), (" 1", 1), ("1.5", 1), ("abc", 0),
+                                    ("-1", 2), ("+1", 1), ("", 0), ("7", 2)])
+def test_m1_softmax_variant_is_read_like_the_reference_binding(env, um, monkeypatch):
+    """MXFA_M1_UM parsed as C atoi, 0 and 1 honoured, else 2 (m1_binding.cpp:100-105)."""
+    from mxflashattn_b200 import m1
+
+    if env is None:
+        monkeypatch.delenv("MXFA_M1_UM", raising=False)
+    else:
+        monkeypatch.setenv("MXFA_M1_UM", env)
+    assert m1.softmax_variant_from_env() == um
