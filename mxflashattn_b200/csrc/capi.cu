@@ -666,6 +666,7 @@ int mxfa_kvcache_attention_ordered_launch(const void* q, const void* k_cache, co
 
 size_t mxfa_cp_buffer_bytes(int world, int B, int HQ, int HKV, int D) {
   if (world <= 0 || B <= 0 || HKV <= 0 || HQ <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return 0;
+  if (static_cast<long long>(B) * HQ > INT_MAX) return 0;
   return cp_layout(world, B * HQ, D).bytes;
 }
 
@@ -807,6 +808,8 @@ int mxfa_cp_merge_launch(void* local_buf, void* out, float* lse, int world, int 
   if (world < 1 || world > 32) return fail(MXFA_ERR_INVALID, "world %d outside 1..32 ranks", world);
   if (HKV <= 0 || HQ % HKV != 0 || (D != 64 && D != 128)) return fail(MXFA_ERR_INVALID, "bad geometry");
   if (B <= 0) return MXFA_OK;
+  if (static_cast<long long>(B) * HQ > INT_MAX)
+    return fail(MXFA_ERR_UNSUPPORTED, "%lld query rows (B*HQ) above 2^31-1", static_cast<long long>(B) * HQ);
   const int rows = B * HQ;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((rows + 3) / 4);

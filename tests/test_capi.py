@@ -164,6 +164,8 @@ def test_guards_refuse_bad_geometry_and_alignment_before_any_device_work(lib):
     assert lib.mxfa_split_combine_launch(A, A + 2, A, None, None, 4, 128, 2, 1, None) == inv
     assert lib.mxfa_split_combine_launch(A, A, A + 2, None, None, 4, 128, 2, 1, None) == inv
     assert lib.mxfa_lse_merge_launch(A + 2, A, None, 2, 4, 128, 1, None) == inv
+    assert lib.mxfa_cp_buffer_bytes(2, 1 << 20, 1 << 12, 8, 128) == 0
+    assert lib.mxfa_cp_merge_launch(A, A, None, 2, 1 << 20, 1 << 12, 8, 128, 1, None) == uns
 
 
 def test_split_plan_invariants(lib):
